@@ -1,0 +1,325 @@
+// Decode attention over the device KV cache, row softmax and row argmax.
+//
+// Reference: the host NumPy attention of orchard/model.py:112-144 (per sequence, per head,
+// softmax(q.K / sqrt(hd)) . V over positions 0..pos, the current token appended first) and
+// the Metal softmax of orchard/kernels/softmax.metal:4-56.
+//
+// Cache layout [slot][head][max_seq][head_dim] fp16: one (slot, head) pair is a contiguous
+// run of pos+1 rows of head_dim halves, so both passes stream whole 32-byte sectors.
+// A CTA owns one (row, head) and a range of positions; with few rows (B = 1) the positions
+// are split over several CTAs and their (max, sum, acc) partials are merged by a second
+// small kernel (flash-decoding). Split partials live in a caller-provided workspace.
+#include <algorithm>
+
+#include "orch_common.cuh"
+
+namespace orch {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnChunk = 1024;  // positions per CTA at most (scores live in shared memory)
+
+struct AttnArgs {
+  const __half* q;
+  const __half* kc;
+  const __half* vc;
+  const int* pos;
+  const int* slots;
+  __half* out;
+  float* ws;  // [M*nh][S][HD + 2]
+  int M, nh, max_seq, S;
+  uint32_t* check;
+};
+
+// VPL consecutive halves (VPL = 1, 2, 4) as floats, one load.
+template <int VPL>
+__device__ __forceinline__ void load_v(const __half* p, float (&f)[VPL]) {
+  if (VPL == 4) {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 a = __half22float2(bits_h2(raw.x)), b = __half22float2(bits_h2(raw.y));
+    f[0] = a.x; f[1] = a.y; f[2 % VPL] = b.x; f[3 % VPL] = b.y;
+  } else if (VPL == 2) {
+    const float2 a = __half22float2(bits_h2(__ldg(reinterpret_cast<const unsigned int*>(p))));
+    f[0] = a.x; f[1 % VPL] = a.y;
+  } else {
+    f[0] = __half2float(p[0]);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+  constexpr int VPL = HD / 32;  // dims per lane in the P.V pass
+  __shared__ float qs[HD];
+  __shared__ float sc[kAttnChunk];
+  __shared__ float red[32];
+  __shared__ float accs[kAttnThreads / 32][HD];
+
+  const int mh = blockIdx.x;
+  const int m = mh / a.nh, h = mh - m * a.nh;
+  const int split = blockIdx.y;
+  const int p = a.pos[m];
+  if (p < 0 || p >= a.max_seq) {  // uniform per CTA
+    if (threadIdx.x == 0) atomicOr(a.check, 2u);
+    return;
+  }
+  const int L = p + 1;
+  const int per = (L + a.S - 1) / a.S;
+  const int p0 = split * per;
+  const int p1 = min(L, p0 + per);
+  const int slot = a.slots ? a.slots[m] : m;
+  const size_t base = ((size_t)slot * a.nh + h) * a.max_seq * HD;
+  const __half* K = a.kc + base;
+  const __half* V = a.vc + base;
+  const float scale = rsqrtf((float)HD);
+
+  for (int d = threadIdx.x; d < HD; d += kAttnThreads)
+    qs[d] = __half2float(a.q[(size_t)m * a.nh * HD + h * HD + d]) * scale;
+  __syncthreads();
+
+  // pass 1: one position per thread, full-row dot product (row = HD halves)
+  float lmax = -INFINITY;
+  for (int t = p0 + threadIdx.x; t < p1; t += kAttnThreads) {
+    const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)t * HD);
+    float s = 0.f;
+#pragma unroll
+    for (int v = 0; v < HD / 8; ++v) {
+      const uint4 raw = __ldg(kr + v);
+      const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(hp[e]);
+        s = fmaf(f.x, qs[v * 8 + 2 * e], s);
+        s = fmaf(f.y, qs[v * 8 + 2 * e + 1], s);
+      }
+    }
+    sc[t - p0] = s;
+    lmax = fmaxf(lmax, s);
+  }
+  const float mx = block_max(lmax, red);
+  float lsum = 0.f;
+  for (int t = threadIdx.x; t < p1 - p0; t += kAttnThreads) {
+    const float e = __expf(sc[t] - mx);
+    sc[t] = e;
+    lsum += e;
+  }
+  const float sum = block_sum(lsum, red);  // contains __syncthreads: sc[] complete
+
+  // pass 2: warp w takes positions w, w+4, ...; lane owns VPL consecutive dims
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float acc[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
+  int t = p0 + warp;
+  for (; t + 3 * (kAttnThreads / 32) < p1; t += 4 * (kAttnThreads / 32)) {
+    float w[4];
+    float vv[4][VPL];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int tq = t + q * (kAttnThreads / 32);
+      w[q] = sc[tq - p0];
+      load_v<VPL>(V + (size_t)tq * HD + lane * VPL, vv[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) acc[i] = fmaf(w[q], vv[q][i], acc[i]);
+  }
+  for (; t < p1; t += kAttnThreads / 32) {
+    const float w = sc[t - p0];
+    float vv[VPL];
+    load_v<VPL>(V + (size_t)t * HD + lane * VPL, vv);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) acc[i] = fmaf(w, vv[i], acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) accs[warp][lane * VPL + i] = acc[i];
+  __syncthreads();
+  for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
+    float v = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < kAttnThreads / 32; ++w2) v += accs[w2][d];
+    if (a.S == 1) {
+      a.out[(size_t)m * a.nh * HD + h * HD + d] = __float2half_rn(v / sum);
+    } else {
+      float* wp = a.ws + ((size_t)mh * a.S + split) * (HD + 2);
+      wp[2 + d] = v;
+      if (d == 0) {
+        wp[0] = (p1 > p0) ? mx : -INFINITY;
+        wp[1] = (p1 > p0) ? sum : 0.f;
+      }
+    }
+  }
+}
+
+template <int HD>
+__global__ void attn_combine_kernel(const AttnArgs a) {
+  const int mh = blockIdx.x;
+  const int m = mh / a.nh, h = mh - m * a.nh;
+  const int p = a.pos[m];
+  if (p < 0 || p >= a.max_seq) return;
+  const float* wp = a.ws + (size_t)mh * a.S * (HD + 2);
+  float gmax = -INFINITY;
+  for (int s = 0; s < a.S; ++s) gmax = fmaxf(gmax, wp[s * (HD + 2)]);
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < a.S; ++s) {
+      const float ms = wp[s * (HD + 2)];
+      if (ms == -INFINITY) continue;
+      const float f = __expf(ms - gmax);
+      den += f * wp[s * (HD + 2) + 1];
+      num += f * wp[s * (HD + 2) + 2 + d];
+    }
+    a.out[(size_t)m * a.nh * HD + h * HD + d] = __float2half_rn(num / den);
+  }
+}
+
+static int attn_splits(int M, int nh, int max_seq) {
+  // enough CTAs to cover the SMs a few times; positions per CTA <= kAttnChunk
+  const int pairs = M * nh;
+  int S = std::max(1, (4 * num_sms() + pairs - 1) / pairs);
+  S = std::max(S, (max_seq + kAttnChunk - 1) / kAttnChunk);
+  return std::min(S, std::max(1, (max_seq + 31) / 32));
+}
+
+template <int HD>
+static int attn_launch(AttnArgs a, cudaStream_t st) {
+  dim3 grid(a.M * a.nh, a.S);
+  attn_decode_kernel<HD><<<grid, kAttnThreads, 0, st>>>(a);
+  if (a.S > 1) attn_combine_kernel<HD><<<a.M * a.nh, HD, 0, st>>>(a);
+  return check_launch("attention_decode");
+}
+
+// ---- row softmax (softmax.metal:4-56), any cols -------------------------------------------
+template <typename TI, typename TO>
+__global__ void softmax_rows_kernel(const TI* in, TO* out, int cols) {
+  __shared__ float red[32];
+  const TI* r = in + (size_t)blockIdx.x * cols;
+  TO* o = out + (size_t)blockIdx.x * cols;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) mx = fmaxf(mx, to_f32(r[i]));
+  mx = block_max(mx, red);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) s += __expf(to_f32(r[i]) - mx);
+  s = block_sum(s, red);
+  const float inv = 1.0f / s;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) o[i] = from_f32<TO>(__expf(to_f32(r[i]) - mx) * inv);
+}
+
+// ---- row argmax (first index of the maximum, as np.argmax) ---------------------------------
+__global__ void argmax_rows_kernel(const float* logits, int V, int* out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const float* r = logits + (size_t)blockIdx.x * V;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = r[i];
+    if (v > best || (v == best && i < bi) || (v != v && best == best)) {  // NaN wins, as np.argmax
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[wid] = best;
+    si[wid] = bi;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+}  // namespace orch
+
+using namespace orch;
+
+extern "C" size_t orch_attention_workspace_bytes(uint32_t M, uint32_t num_heads, uint32_t head_dim,
+                                                 uint32_t max_seq) {
+  if (M == 0 || num_heads == 0 || max_seq == 0) return 0;
+  const int S = attn_splits((int)M, (int)num_heads, (int)max_seq);
+  return S > 1 ? (size_t)M * num_heads * S * (head_dim + 2) * sizeof(float) : 0;
+}
+
+extern "C" int orch_attention_decode(const void* q, const void* k_cache, const void* v_cache,
+                                     const int32_t* pos, const int32_t* slots, void* out, uint32_t M,
+                                     uint32_t num_heads, uint32_t head_dim, uint32_t max_seq,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return ORCH_OK;
+  ORCH_REQUIRE(q && k_cache && v_cache && pos && out, "attention_decode: null pointer");
+  ORCH_REQUIRE(num_heads > 0 && max_seq > 0, "attention_decode: empty shape");
+  ORCH_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
+               "attention_decode: head_dim must be 32, 64 or 128");
+  AttnArgs a;
+  a.q = static_cast<const __half*>(q);
+  a.kc = static_cast<const __half*>(k_cache);
+  a.vc = static_cast<const __half*>(v_cache);
+  a.pos = pos;
+  a.slots = slots;
+  a.out = static_cast<__half*>(out);
+  a.M = (int)M;
+  a.nh = (int)num_heads;
+  a.max_seq = (int)max_seq;
+  a.S = attn_splits(a.M, a.nh, a.max_seq);
+  a.check = device_check_word();
+  const size_t need = orch_attention_workspace_bytes(M, num_heads, head_dim, max_seq);
+  ORCH_REQUIRE(workspace_bytes >= need && (need == 0 || workspace != nullptr),
+               "attention_decode: workspace too small");
+  a.ws = static_cast<float*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  switch (head_dim) {
+    case 32: return attn_launch<32>(a, st);
+    case 64: return attn_launch<64>(a, st);
+    default: return attn_launch<128>(a, st);
+  }
+}
+
+extern "C" int orch_softmax_ex(const void* in, int in_dt, void* out, int out_dt, uint32_t rows,
+                               uint32_t cols, void* stream) {
+  if (rows == 0 || cols == 0) return ORCH_OK;
+  ORCH_REQUIRE(in && out, "softmax: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const int th = cols >= 1024 ? 1024 : cols >= 256 ? 256 : 128;
+  if (in_dt == ORCH_F16 && out_dt == ORCH_F16)
+    softmax_rows_kernel<__half, __half><<<rows, th, 0, st>>>((const __half*)in, (__half*)out, cols);
+  else if (in_dt == ORCH_F32 && out_dt == ORCH_F32)
+    softmax_rows_kernel<float, float><<<rows, th, 0, st>>>((const float*)in, (float*)out, cols);
+  else if (in_dt == ORCH_F16 && out_dt == ORCH_F32)
+    softmax_rows_kernel<__half, float><<<rows, th, 0, st>>>((const __half*)in, (float*)out, cols);
+  else if (in_dt == ORCH_F32 && out_dt == ORCH_F16)
+    softmax_rows_kernel<float, __half><<<rows, th, 0, st>>>((const float*)in, (__half*)out, cols);
+  else
+    return fail(ORCH_ERR_INVALID, "softmax: bad dtype");
+  return check_launch("softmax");
+}
+
+extern "C" int orch_softmax(const void* in, void* out, uint32_t rows, uint32_t cols, void* stream) {
+  return orch_softmax_ex(in, ORCH_F16, out, ORCH_F16, rows, cols, stream);
+}
+
+extern "C" int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, void* stream) {
+  if (M == 0) return ORCH_OK;
+  ORCH_REQUIRE(logits && out && V > 0, "argmax_rows: bad arguments");
+  argmax_rows_kernel<<<M, 1024, 0, as_stream(stream)>>>(logits, (int)V, out);
+  return check_launch("argmax_rows");
+}

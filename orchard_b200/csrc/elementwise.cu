@@ -1,0 +1,320 @@
+// RMSNorm, RoPE, add/mul/SiLU, embedding gathers and the fp32/fp16 dense matmuls of the
+// reference operator surface.
+//
+// Reference kernels: orchard/kernels/rmsnorm.metal:4-36 (one thread per row there; here
+// one CTA per row with a warp-shuffle reduction), rope.metal:4-50 (interleaved pairs; here
+// each row uses its own row of angles), elementwise.metal:4-30, embedding.metal:4-17,
+// matmul.metal:4-23, matmul_simd.metal:4-40. All arithmetic is fp32; half tensors are
+// converted on load and rounded once on store.
+#include "orch_common.cuh"
+
+namespace orch {
+
+// ---- RMSNorm ---------------------------------------------------------------------------
+template <typename TI, typename TW, typename TO>
+__global__ void rmsnorm_kernel(const TI* in, const TW* w, TO* out, float eps, int N) {
+  __shared__ float red[32];
+  const TI* r = in + (size_t)blockIdx.x * N;
+  TO* o = out + (size_t)blockIdx.x * N;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const float v = to_f32(r[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)N + eps);
+  for (int i = threadIdx.x; i < N; i += blockDim.x) o[i] = from_f32<TO>(to_f32(r[i]) * inv * to_f32(w[i]));
+}
+
+// ---- RoPE: in/out [rows, heads, hd], cos/sin [rows, hd/2] ---------------------------------
+template <typename TI, typename TT, typename TO>
+__global__ void rope_kernel(const TI* in, const TT* cs, const TT* sn, TO* out, int hd, int heads,
+                            int rows) {
+  const int half = hd >> 1;
+  const size_t total = (size_t)rows * heads * half;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int pi = (int)(i % half);
+    const size_t rh = i / half;
+    const int row = (int)(rh / heads);
+    const size_t b = rh * hd + 2 * pi;
+    const float x0 = to_f32(in[b]), x1 = to_f32(in[b + 1]);
+    const float c = to_f32(cs[(size_t)row * half + pi]), s = to_f32(sn[(size_t)row * half + pi]);
+    const float o0 = x0 * c - x1 * s;
+    const float o1 = x0 * s + x1 * c;
+    out[b] = from_f32<TO>(o0);
+    out[b + 1] = from_f32<TO>(o1);
+  }
+}
+
+// ---- elementwise -------------------------------------------------------------------------
+template <typename T, int OP>
+__global__ void binary_kernel(const T* a, const T* b, T* c, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float x = to_f32(a[i]), y = to_f32(b[i]);
+    c[i] = from_f32<T>(OP == 0 ? x + y : x * y);
+  }
+}
+
+template <typename T>
+__global__ void silu_kernel(const T* in, T* out, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float x = to_f32(in[i]);
+    out[i] = from_f32<T>(x / (1.0f + expf(-x)));
+  }
+}
+
+// ---- embedding gathers ---------------------------------------------------------------------
+template <typename TW, typename TO>
+__global__ void embedding_kernel(const int* ids, const TW* w, TO* out, int tokens, int hd, int vocab,
+                                 uint32_t* check) {
+  const size_t total = (size_t)tokens * hd;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / hd), d = (int)(i % hd);
+    const int id = ids[t];
+    if (id < 0 || id >= vocab) {
+      out[i] = from_f32<TO>(0.f);
+      if (d == 0) atomicOr(check, 4u);
+      continue;
+    }
+    out[i] = from_f32<TO>(to_f32(w[(size_t)id * hd + d]));
+  }
+}
+
+// ---- dense matmuls (surface): C[M,N] = A[M,K] B[K,N], 64x64 tiles, 4x4 per thread --------
+template <typename T>
+__global__ void __launch_bounds__(256) matmul_kernel(const T* A, const T* B, T* C, int M, int N, int K) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int r = i / 16, kk = i % 16;  // A tile [64 rows][16 k]
+      const int gm = m0 + r, gk = k0 + kk;
+      As[kk][r] = (gm < M && gk < K) ? to_f32(A[(size_t)gm * K + gk]) : 0.f;
+      const int kb = i / 64, cn = i % 64;  // B tile [16 k][64 cols]
+      const int gk2 = k0 + kb, gn = n0 + cn;
+      Bs[kb][cn] = (gk2 < K && gn < N) ? to_f32(B[(size_t)gk2 * N + gn]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
+      if (gm < M && gn < N) C[(size_t)gm * N + gn] = from_f32<T>(acc[i][j]);
+    }
+}
+
+static int grid_for(size_t n, int block) {
+  const size_t g = (n + block - 1) / block;
+  const size_t cap = (size_t)num_sms() * 16;
+  return (int)(g < cap ? (g ? g : 1) : cap);
+}
+
+}  // namespace orch
+
+using namespace orch;
+
+#define DT_OK(dt) ((dt) == ORCH_F32 || (dt) == ORCH_F16)
+
+extern "C" int orch_rmsnorm_ex(const void* in, int in_dt, const void* weight, int w_dt, void* out,
+                               int out_dt, float eps, uint32_t N, uint32_t count, void* stream) {
+  if (count == 0) return ORCH_OK;
+  ORCH_REQUIRE(in && weight && out && N > 0, "rmsnorm: bad arguments");
+  ORCH_REQUIRE(DT_OK(in_dt) && DT_OK(w_dt) && DT_OK(out_dt), "rmsnorm: bad dtype");
+  cudaStream_t st = as_stream(stream);
+  const int th = N >= 1024 ? 256 : 128;
+#define RMS_CASE(TI, TW, TO)                                                                   \
+  rmsnorm_kernel<TI, TW, TO><<<count, th, 0, st>>>((const TI*)in, (const TW*)weight, (TO*)out, \
+                                                   eps, (int)N)
+  const int key = in_dt * 4 + w_dt * 2 + out_dt;
+  switch (key) {
+    case 0: RMS_CASE(float, float, float); break;
+    case 1: RMS_CASE(float, float, __half); break;
+    case 2: RMS_CASE(float, __half, float); break;
+    case 3: RMS_CASE(float, __half, __half); break;
+    case 4: RMS_CASE(__half, float, float); break;
+    case 5: RMS_CASE(__half, float, __half); break;
+    case 6: RMS_CASE(__half, __half, float); break;
+    default: RMS_CASE(__half, __half, __half); break;
+  }
+#undef RMS_CASE
+  return check_launch("rmsnorm");
+}
+
+extern "C" int orch_rmsnorm(const void* in, const void* weight, void* out, float eps, uint32_t N,
+                            uint32_t count, void* stream) {
+  return orch_rmsnorm_ex(in, ORCH_F16, weight, ORCH_F16, out, ORCH_F16, eps, N, count, stream);
+}
+
+extern "C" int orch_rope_ex(const void* in, int in_dt, const void* cs, const void* sn, int tab_dt,
+                            void* out, int out_dt, uint32_t head_dim, uint32_t num_heads,
+                            uint32_t seq_len, void* stream) {
+  if (seq_len == 0 || num_heads == 0) return ORCH_OK;
+  ORCH_REQUIRE(in && cs && sn && out, "rope: null pointer");
+  ORCH_REQUIRE(head_dim >= 2 && head_dim % 2 == 0, "rope: head_dim must be even");
+  ORCH_REQUIRE(DT_OK(in_dt) && DT_OK(tab_dt) && DT_OK(out_dt), "rope: bad dtype");
+  cudaStream_t st = as_stream(stream);
+  const size_t n = (size_t)seq_len * num_heads * (head_dim / 2);
+  const int g = grid_for(n, 256);
+#define ROPE_CASE(TI, TT, TO)                                                                 \
+  rope_kernel<TI, TT, TO><<<g, 256, 0, st>>>((const TI*)in, (const TT*)cs, (const TT*)sn, (TO*)out, \
+                                             (int)head_dim, (int)num_heads, (int)seq_len)
+  const int key = in_dt * 4 + tab_dt * 2 + out_dt;
+  switch (key) {
+    case 0: ROPE_CASE(float, float, float); break;
+    case 1: ROPE_CASE(float, float, __half); break;
+    case 2: ROPE_CASE(float, __half, float); break;
+    case 3: ROPE_CASE(float, __half, __half); break;
+    case 4: ROPE_CASE(__half, float, float); break;
+    case 5: ROPE_CASE(__half, float, __half); break;
+    case 6: ROPE_CASE(__half, __half, float); break;
+    default: ROPE_CASE(__half, __half, __half); break;
+  }
+#undef ROPE_CASE
+  return check_launch("rope");
+}
+
+extern "C" int orch_rope(const void* in, const void* cs, const void* sn, void* out, uint32_t head_dim,
+                         uint32_t num_heads, uint32_t seq_len, void* stream) {
+  return orch_rope_ex(in, ORCH_F16, cs, sn, ORCH_F16, out, ORCH_F16, head_dim, num_heads, seq_len, stream);
+}
+
+extern "C" int orch_binary_ex(int op, const void* a, const void* b, void* c, int dt, uint32_t size,
+                              void* stream) {
+  if (size == 0) return ORCH_OK;
+  ORCH_REQUIRE(a && b && c, "binary: null pointer");
+  ORCH_REQUIRE(op == 0 || op == 1, "binary: op must be 0 (add) or 1 (mul)");
+  ORCH_REQUIRE(DT_OK(dt), "binary: bad dtype");
+  cudaStream_t st = as_stream(stream);
+  const int g = grid_for(size, 256);
+  if (dt == ORCH_F16) {
+    if (op == 0) binary_kernel<__half, 0><<<g, 256, 0, st>>>((const __half*)a, (const __half*)b, (__half*)c, size);
+    else binary_kernel<__half, 1><<<g, 256, 0, st>>>((const __half*)a, (const __half*)b, (__half*)c, size);
+  } else {
+    if (op == 0) binary_kernel<float, 0><<<g, 256, 0, st>>>((const float*)a, (const float*)b, (float*)c, size);
+    else binary_kernel<float, 1><<<g, 256, 0, st>>>((const float*)a, (const float*)b, (float*)c, size);
+  }
+  return check_launch("binary");
+}
+
+extern "C" int orch_add(const void* a, const void* b, void* c, uint32_t size, void* stream) {
+  return orch_binary_ex(0, a, b, c, ORCH_F16, size, stream);
+}
+extern "C" int orch_mul(const void* a, const void* b, void* c, uint32_t size, void* stream) {
+  return orch_binary_ex(1, a, b, c, ORCH_F16, size, stream);
+}
+
+extern "C" int orch_silu_ex(const void* in, void* out, int dt, uint32_t size, void* stream) {
+  if (size == 0) return ORCH_OK;
+  ORCH_REQUIRE(in && out, "silu: null pointer");
+  ORCH_REQUIRE(DT_OK(dt), "silu: bad dtype");
+  cudaStream_t st = as_stream(stream);
+  const int g = grid_for(size, 256);
+  if (dt == ORCH_F16) silu_kernel<__half><<<g, 256, 0, st>>>((const __half*)in, (__half*)out, size);
+  else silu_kernel<float><<<g, 256, 0, st>>>((const float*)in, (float*)out, size);
+  return check_launch("silu");
+}
+extern "C" int orch_silu(const void* in, void* out, uint32_t size, void* stream) {
+  return orch_silu_ex(in, out, ORCH_F16, size, stream);
+}
+
+extern "C" int orch_embedding_ex(const void* ids, const void* weights, int w_dt, void* out, int out_dt,
+                                 uint32_t num_tokens, uint32_t hidden_dim, uint32_t vocab, void* stream) {
+  if (num_tokens == 0 || hidden_dim == 0) return ORCH_OK;
+  ORCH_REQUIRE(ids && weights && out, "embedding: null pointer");
+  ORCH_REQUIRE(vocab > 0, "embedding: vocab must be positive");
+  ORCH_REQUIRE(DT_OK(w_dt) && DT_OK(out_dt), "embedding: bad dtype");
+  cudaStream_t st = as_stream(stream);
+  const size_t n = (size_t)num_tokens * hidden_dim;
+  const int g = grid_for(n, 256);
+  uint32_t* chk = device_check_word();
+  const int* id = (const int*)ids;
+  if (w_dt == ORCH_F16 && out_dt == ORCH_F16)
+    embedding_kernel<__half, __half><<<g, 256, 0, st>>>(id, (const __half*)weights, (__half*)out, num_tokens, hidden_dim, vocab, chk);
+  else if (w_dt == ORCH_F16)
+    embedding_kernel<__half, float><<<g, 256, 0, st>>>(id, (const __half*)weights, (float*)out, num_tokens, hidden_dim, vocab, chk);
+  else if (out_dt == ORCH_F16)
+    embedding_kernel<float, __half><<<g, 256, 0, st>>>(id, (const float*)weights, (__half*)out, num_tokens, hidden_dim, vocab, chk);
+  else
+    embedding_kernel<float, float><<<g, 256, 0, st>>>(id, (const float*)weights, (float*)out, num_tokens, hidden_dim, vocab, chk);
+  return check_launch("embedding");
+}
+
+extern "C" int orch_embedding(const void* ids, const void* weights, void* out, uint32_t num_tokens,
+                              uint32_t hidden_dim, uint32_t vocab, void* stream) {
+  return orch_embedding_ex(ids, weights, ORCH_F16, out, ORCH_F16, num_tokens, hidden_dim, vocab, stream);
+}
+
+extern "C" int orch_embed_rows(const int32_t* ids, const void* table, int table_dt, float* x, uint32_t M,
+                               uint32_t H, uint32_t V, void* stream) {
+  return orch_embedding_ex(ids, table, table_dt, x, ORCH_F32, M, H, V, stream);
+}
+
+extern "C" int orch_matmul(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                           void* stream) {
+  if (M == 0 || N == 0) return ORCH_OK;
+  ORCH_REQUIRE(a && b && c, "matmul: null pointer");
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  matmul_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(a, b, c, (int)M, (int)N, (int)K);
+  return check_launch("matmul");
+}
+
+extern "C" int orch_matmul_simd(const void* a, const void* b, void* c, uint32_t M, uint32_t N, uint32_t K,
+                                void* stream) {
+  if (M == 0 || N == 0) return ORCH_OK;
+  ORCH_REQUIRE(a && b && c, "matmul_simd: null pointer");
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  matmul_kernel<__half><<<grid, 256, 0, as_stream(stream)>>>((const __half*)a, (const __half*)b, (__half*)c,
+                                                            (int)M, (int)N, (int)K);
+  return check_launch("matmul_simd");
+}
+
+// ---- LoRA down-projection t[m, :] = x[m, :] . A   (x fp16 [M,K], A fp32 [K,R]) -------------
+namespace orch {
+__global__ void __launch_bounds__(256) lora_xa_kernel(const __half* x, const float* A, float* t, int K, int R) {
+  __shared__ float part[8][33];
+  const int m = blockIdx.x;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const __half* xr = x + (size_t)m * K;
+  for (int j0 = 0; j0 < R; j0 += 32) {
+    const int j = j0 + tx;
+    float acc = 0.f;
+    if (j < R)
+      for (int k = ty; k < K; k += 8) acc = fmaf(__half2float(xr[k]), A[(size_t)k * R + j], acc);
+    part[ty][tx] = acc;
+    __syncthreads();
+    if (ty == 0 && j < R) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += part[i][tx];
+      t[(size_t)m * R + j] = s;
+    }
+    __syncthreads();
+  }
+}
+}  // namespace orch
+
+extern "C" int orch_lora_xa(const void* x, const float* a, float* t, uint32_t M, uint32_t K, uint32_t R,
+                            void* stream) {
+  if (M == 0 || R == 0) return ORCH_OK;
+  ORCH_REQUIRE(x && a && t && K > 0, "lora_xa: bad arguments");
+  orch::lora_xa_kernel<<<M, 256, 0, as_stream(stream)>>>((const __half*)x, a, t, (int)K, (int)R);
+  return check_launch("lora_xa");
+}

@@ -1,0 +1,417 @@
+"""Llama decode on B200: the reference's Python API over the fused sm_100a kernels.
+
+Reference API: ``orchard.Llama(model_path)``, ``load_lora``, ``generate_batch(prompts,
+max_tokens=50, temperature=0.7)`` (orchard/model.py:197-381). Arithmetic follows
+``LlamaLayer.forward`` (orchard/model.py:78-195); the per-layer sequence of the
+reference's ~14 synchronous ops plus host attention becomes five launches:
+
+  1. RMSNorm (fp32 residual -> fp16)                          rmsnorm.metal
+  2. Q/K/V INT4 projection + LoRA + RoPE + KV-cache append     model.py:94-124
+  3. attention over the device KV cache                        model.py:117-137
+  4. O INT4 projection + LoRA + residual add                   model.py:147-157
+  5. RMSNorm, gate/up INT4 projection + LoRA + SwiGLU, down projection + residual
+     (three launches)                                          model.py:160-193
+
+then final RMSNorm, the INT4 lm_head and a row argmax. A whole decode step for a batch
+size is captured once in a CUDA graph and replayed.
+
+Token flow of ``generate_batch`` is the reference's: prompts are prefilled one position
+at a time (all sequences of the batch together), the last prompt token is fed again as
+the first decode input at position ``len(prompt)`` (orchard/model.py:305,325-329), the
+next token is the argmax for temperature 0 and ``np.random.choice`` over
+``softmax(logits / T)`` otherwise (orchard/model.py:244-252), and id 2 ends a row.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import F16, F32, call, ptr
+from .loader import Checkpoint, from_tensors, load_checkpoint, load_lora
+
+EOS_ID = 2
+
+
+@dataclass
+class LlamaConfig:
+    hidden_size: int
+    num_attention_heads: int
+    intermediate_size: int
+    num_hidden_layers: int
+    vocab_size: int
+    rms_norm_eps: float = 1e-5
+    max_position_embeddings: int = 2048
+    rope_theta: float = 10000.0
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "LlamaConfig":
+        return cls(hidden_size=d["hidden_size"], num_attention_heads=d["num_attention_heads"],
+                   intermediate_size=d["intermediate_size"],
+                   num_hidden_layers=d["num_hidden_layers"], vocab_size=d["vocab_size"],
+                   rms_norm_eps=d.get("rms_norm_eps", 1e-5),
+                   max_position_embeddings=d.get("max_position_embeddings", 2048),
+                   rope_theta=d.get("rope_theta", 10000.0))
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+
+def precompute_freqs_cis(dim: int, end: int, theta: float = 10000.0):
+    """float32 cos/sin tables ``[end, dim/2]`` computed exactly as orchard/model.py:7-13."""
+    inv = 1.0 / (theta ** (np.arange(0, dim, 2)[: dim // 2].astype(np.float32) / dim))
+    ang = np.outer(np.arange(end).astype(np.float32), inv)
+    return np.cos(ang), np.sin(ang)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+# --------------------------------------------------------------------------------------
+# device weights
+# --------------------------------------------------------------------------------------
+
+def quantize_on_device(w, device) -> tuple:
+    """Reference INT4 packing (orchard/quantizer.py:3-78) on the GPU: returns
+    ``(packed uint8 [N, K/2], scales fp16 [N, K/32])`` device tensors, bit-identical to
+    the host packer for fp32 input or fp16 input cast to fp32 (the loader's cast)."""
+    t = torch.as_tensor(w).to(device)
+    if t.dtype not in (torch.float16, torch.float32):
+        t = t.float()
+    t = t.contiguous()
+    n, k = t.shape
+    packed = torch.empty((n, k // 2), dtype=torch.uint8, device=device)
+    scales = torch.empty((n, k // 32), dtype=torch.float16, device=device)
+    call("orch_quantize_q4_0", ptr(t), F16 if t.dtype == torch.float16 else F32, ptr(packed),
+         ptr(scales), n, k, _stream())
+    return packed, scales
+
+
+def _packed_on_device(entry, device) -> tuple:
+    if entry[0] == "packed":
+        p = torch.as_tensor(np.ascontiguousarray(entry[1]).view(np.uint8)).to(device)
+        s = torch.as_tensor(np.ascontiguousarray(entry[2]).astype(np.float16)).to(device)
+        return p, s
+    return quantize_on_device(entry[1], device)
+
+
+def interleave_gate_up(p1, s1, p3, s3):
+    """Rows of gate (w1) and up (w3) interleaved in blocks of 16: rows 32b..32b+15 = gate
+    16b..16b+15, rows 32b+16..32b+31 = up 16b..16b+15 (the SwiGLU epilogue's layout)."""
+    F = p1.shape[0]
+    assert F % 16 == 0 and p3.shape[0] == F
+
+    def il(a, b):
+        return torch.stack([a.view(F // 16, 16, -1), b.view(F // 16, 16, -1)], dim=1).reshape(2 * F, -1)
+
+    return il(p1, p3).contiguous(), il(s1, s3).contiguous()
+
+
+class DeviceLayer:
+    def __init__(self, entries: dict, cfg: LlamaConfig, device):
+        H, F = cfg.hidden_size, cfg.intermediate_size
+        q = {n: _packed_on_device(entries[n], device) for n in ("wq", "wk", "wv", "wo", "w1", "w3", "w2")}
+        self.wqkv = torch.cat([q["wq"][0], q["wk"][0], q["wv"][0]]).contiguous()
+        self.sqkv = torch.cat([q["wq"][1], q["wk"][1], q["wv"][1]]).contiguous()
+        self.wo, self.so = q["wo"]
+        self.w13, self.s13 = interleave_gate_up(q["w1"][0], q["w1"][1], q["w3"][0], q["w3"][1])
+        self.w2, self.s2 = q["w2"]
+        self.attn_norm = torch.as_tensor(np.asarray(entries["attn_norm"], np.float32)).to(device)
+        self.ffn_norm = torch.as_tensor(np.asarray(entries["ffn_norm"], np.float32)).to(device)
+        assert self.wqkv.shape == (3 * H, H // 2) and self.w13.shape == (2 * F, H // 2)
+        assert self.w2.shape == (H, F // 2)
+        self.lora: Dict[str, tuple] = {}
+
+    def weight_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in
+                   (self.wqkv, self.sqkv, self.wo, self.so, self.w13, self.s13, self.w2, self.s2))
+
+    def set_lora(self, mods: Dict[str, tuple], cfg: LlamaConfig, r: int, device):
+        """Packs adapters per fused projection: A_cat [K, R*r] and B_cat [R, r, width]."""
+        H, F = cfg.hidden_size, cfg.intermediate_size
+        groups = {"qkv": (("wq", "wk", "wv"), H, H), "o": (("wo",), H, H),
+                  "gu": (("w1", "w3"), H, F), "down": (("w2",), F, H)}
+        self.lora = {}
+        for g, (names, k_in, width) in groups.items():
+            if not any(n in mods for n in names):
+                continue
+            R = len(names)
+            a = np.zeros((k_in, R * r), np.float32)
+            b = np.zeros((R, r, width), np.float32)
+            for i, n in enumerate(names):
+                if n in mods:
+                    A, Bm = mods[n]
+                    a[:, i * r:(i + 1) * r] = A
+                    b[i] = Bm
+            self.lora[g] = (torch.as_tensor(a).to(device), torch.as_tensor(b).to(device), R)
+
+
+# --------------------------------------------------------------------------------------
+# engine
+# --------------------------------------------------------------------------------------
+
+class DecodeEngine:
+    """Device state for up to ``max_batch`` sequences of up to ``max_seq`` positions."""
+
+    def __init__(self, ck: Checkpoint, device=0, max_batch: int = 32, max_seq: Optional[int] = None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("orchard_b200 needs a CUDA device (there is no CPU fallback)")
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        torch.cuda.set_device(self.device)
+        call("orch_init", self.device.index or 0, None)
+        self.cfg = cfg = LlamaConfig.from_dict(ck.config)
+        if not ck.complete():
+            raise ValueError("checkpoint is missing tensors")
+        H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+        self.max_batch = max_batch
+        self.max_seq = max_seq or cfg.max_position_embeddings
+        self.max_pos = max(self.max_seq, cfg.max_position_embeddings)
+        dev = self.device
+        self.layers = [DeviceLayer(e, cfg, dev) for e in ck.layers]
+        emb = np.asarray(ck.embed)
+        self.embed = torch.as_tensor(emb if emb.dtype in (np.float16, np.float32) else emb.astype(np.float32)).to(dev)
+        self.norm = torch.as_tensor(np.asarray(ck.norm, np.float32)).to(dev)
+        self.lm_w, self.lm_s = _packed_on_device(ck.lm_head, dev)
+        cos, sin = precompute_freqs_cis(cfg.head_dim, self.max_pos, cfg.rope_theta)
+        self.cos = torch.as_tensor(cos).to(dev)
+        self.sin = torch.as_tensor(sin).to(dev)
+        nl, nh, hd = cfg.num_hidden_layers, cfg.num_attention_heads, cfg.head_dim
+        self.k_cache = torch.zeros((nl, max_batch, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        B = max_batch
+        self.x = torch.zeros((B, H), dtype=torch.float32, device=dev)
+        self.xn = torch.zeros((B, H), dtype=torch.float16, device=dev)
+        self.q = torch.zeros((B, H), dtype=torch.float16, device=dev)
+        self.attn = torch.zeros((B, H), dtype=torch.float16, device=dev)
+        self.h = torch.zeros((B, F), dtype=torch.float16, device=dev)
+        self.logits = torch.zeros((B, V), dtype=torch.float32, device=dev)
+        self.tok_in = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.tok_out = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.slots = torch.arange(B, dtype=torch.int32, device=dev)
+        self.lora_r = 0
+        self.lora_t = torch.zeros((B, 3 * 64), dtype=torch.float32, device=dev)
+        ws = _lib.lib().orch_attention_workspace_bytes(B, nh, hd, self.max_seq)
+        self.attn_ws = torch.zeros(max(ws, 16) // 4 + 1, dtype=torch.float32, device=dev)
+        self.attn_ws_bytes = ws
+        self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
+        torch.cuda.synchronize(dev)
+
+    # -- lora --------------------------------------------------------------------------
+    def set_lora(self, per_layer: Dict[int, Dict[str, tuple]], r: int):
+        if r > 64:
+            raise ValueError("LoRA rank above 64 is not supported by the fused epilogues")
+        for li, layer in enumerate(self.layers):
+            layer.set_lora(per_layer.get(li, {}), self.cfg, r, self.device)
+        self.lora_r = r
+        self.graphs.clear()
+
+    def _lora(self, layer, g, x, M, s):
+        if g not in layer.lora:
+            return None, None, 0
+        a, b, R = layer.lora[g]
+        K = a.shape[0]
+        call("orch_lora_xa", ptr(x), ptr(a), ptr(self.lora_t), M, K, R * self.lora_r, s)
+        return ptr(self.lora_t), ptr(b), self.lora_r
+
+    # -- one step ----------------------------------------------------------------------
+    def run_layers(self, M: int):
+        """All layers for rows [0, M): tokens in tok_in, positions in pos."""
+        cfg, s = self.cfg, _stream()
+        H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+        nh, hd, eps = cfg.num_attention_heads, cfg.head_dim, cfg.rms_norm_eps
+        call("orch_embed_rows", ptr(self.tok_in), ptr(self.embed), F16 if self.embed.dtype == torch.float16 else F32,
+             ptr(self.x), M, H, V, s)
+        for li, L in enumerate(self.layers):
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            call("orch_rmsnorm_ex", ptr(self.x), F32, ptr(L.attn_norm), F32, ptr(self.xn), F16, eps, H, M, s)
+            lt, lb, lr = self._lora(L, "qkv", self.xn, M, s)
+            call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(self.xn), M, H, H, nh, ptr(self.pos),
+                 ptr(self.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(self.q), ptr(kc), ptr(vc),
+                 self.max_seq, lt, lb, lr, s)
+            call("orch_attention_decode", ptr(self.q), ptr(kc), ptr(vc), ptr(self.pos), ptr(self.slots),
+                 ptr(self.attn), M, nh, hd, self.max_seq, ptr(self.attn_ws), self.attn_ws_bytes, s)
+            lt, lb, lr = self._lora(L, "o", self.attn, M, s)
+            call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(self.attn), ptr(self.x), M, H, H, lt, lb, lr, s)
+            call("orch_rmsnorm_ex", ptr(self.x), F32, ptr(L.ffn_norm), F32, ptr(self.xn), F16, eps, H, M, s)
+            lt, lb, lr = self._lora(L, "gu", self.xn, M, s)
+            call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(self.xn), ptr(self.h), M, H, F, lt, lb, lr, s)
+            lt, lb, lr = self._lora(L, "down", self.h, M, s)
+            call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(self.h), ptr(self.x), M, F, H, lt, lb, lr, s)
+
+    def run_head(self, M: int):
+        """Final RMSNorm, INT4 lm_head (fp32 logits) and argmax into tok_out."""
+        cfg, s = self.cfg, _stream()
+        H, V = cfg.hidden_size, cfg.vocab_size
+        call("orch_rmsnorm_ex", ptr(self.x), F32, ptr(self.norm), F32, ptr(self.xn), F16, cfg.rms_norm_eps, H, M, s)
+        call("orch_gemm_q4_0_ex", ptr(self.lm_w), ptr(self.lm_s), ptr(self.xn), F16, ptr(self.logits), F32,
+             H, V, M, s)
+        call("orch_argmax_rows", ptr(self.logits), M, V, ptr(self.tok_out), s)
+
+    def kernel_launches_per_step(self, M: int, logits: bool = True) -> int:
+        """Kernels of this library one step launches (for reporting)."""
+        per_layer = 7 + sum(1 for L in self.layers[:1] for _ in L.lora)
+        n = 1 + per_layer * len(self.layers)
+        if _lib.lib().orch_attention_workspace_bytes(M, self.cfg.num_attention_heads, self.cfg.head_dim,
+                                                     self.max_seq) > 0:
+            n += len(self.layers)
+        return n + (3 if logits else 0)
+
+    def step(self, M: int, logits: bool = True, graph: bool = True):
+        """One decode (or prefill) step for rows [0, M); with `graph` the step is replayed
+        from a captured CUDA graph."""
+        key = (M, logits)
+        if not graph:
+            self.run_layers(M)
+            if logits:
+                self.run_head(M)
+            return
+        g = self.graphs.get(key)
+        if g is None:
+            # warm once outside capture (sets kernel attributes), then capture
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.run_layers(M)
+                if logits:
+                    self.run_head(M)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.run_layers(M)
+                if logits:
+                    self.run_head(M)
+            self.graphs[key] = g
+            # capture only records; the step itself still has to run
+        g.replay()
+
+    def reset_cache(self):
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+
+
+# --------------------------------------------------------------------------------------
+# public API
+# --------------------------------------------------------------------------------------
+
+class Llama:
+    """``orchard.Llama`` on B200 (orchard/model.py:197-381)."""
+
+    def __init__(self, model_path: Optional[str] = None, *, checkpoint: Optional[Checkpoint] = None,
+                 device=0, max_batch: int = 32, max_seq: Optional[int] = None, tokenizer=None,
+                 use_graphs: bool = True):
+        ck = checkpoint if checkpoint is not None else load_checkpoint(model_path)
+        self.config = dict(ck.config)
+        self.engine = DecodeEngine(ck, device=device, max_batch=max_batch, max_seq=max_seq)
+        self.use_graphs = use_graphs
+        self.tokenizer = tokenizer
+        if tokenizer is None and model_path is not None:
+            tp = os.path.join(model_path, "tokenizer.json")
+            if os.path.exists(tp):
+                try:
+                    from tokenizers import Tokenizer
+                    self.tokenizer = Tokenizer.from_file(tp)
+                except ImportError:
+                    self.tokenizer = None
+
+    @classmethod
+    def from_tensors(cls, config: dict, tensors: Dict[str, np.ndarray], **kw) -> "Llama":
+        return cls(checkpoint=from_tensors(config, tensors), **kw)
+
+    def load_lora(self, adapter_path: str):
+        per_layer, r, _alpha = load_lora(adapter_path, self.engine.cfg.num_hidden_layers)
+        self.engine.set_lora(per_layer, r)
+
+    # -- sampling (orchard/model.py:244-252) --------------------------------------------
+    @staticmethod
+    def _sample(logits: np.ndarray, temperature: float) -> int:
+        if temperature == 0:
+            return int(np.argmax(logits))
+        logits = logits - np.max(logits)
+        probs = np.exp(logits / temperature) / np.sum(np.exp(logits / temperature))
+        return int(np.random.choice(len(probs), p=probs))
+
+    def generate_batch(self, prompts: List[str], max_tokens: int = 50, temperature: float = 0.7):
+        if self.tokenizer is None:
+            raise RuntimeError("Tokenizer not available")
+        ids = [self.tokenizer.encode(p).ids for p in prompts]
+        out = self.generate_batch_ids(ids, max_tokens=max_tokens, temperature=temperature)
+        return [self.tokenizer.decode(seq) for seq in out]
+
+    def prefill(self, prompt_ids: Sequence[Sequence[int]]):
+        """Fills the KV cache with every prompt, one position per step for all rows
+        (rows past their prompt re-feed their last token; those positions are rewritten
+        by decode before they are read)."""
+        eng = self.engine
+        B = len(prompt_ids)
+        if B > eng.max_batch:
+            raise ValueError(f"batch {B} exceeds max_batch {eng.max_batch}")
+        if any(len(p) == 0 for p in prompt_ids):
+            raise ValueError("empty prompt")
+        longest = max(len(p) for p in prompt_ids)
+        if longest + 1 > eng.max_seq:
+            raise ValueError("prompt longer than the KV cache")
+        eng.reset_cache()
+        toks = np.array([[p[min(i, len(p) - 1)] for p in prompt_ids] for i in range(longest)], np.int32)
+        pos = np.array([[i for _ in prompt_ids] for i in range(longest)], np.int32)
+        toks_d = torch.as_tensor(toks).to(eng.device)
+        pos_d = torch.as_tensor(pos).to(eng.device)
+        for i in range(longest):
+            eng.tok_in[:B].copy_(toks_d[i])
+            eng.pos[:B].copy_(pos_d[i])
+            eng.step(B, logits=False, graph=self.use_graphs)
+
+    def generate_batch_ids(self, prompt_ids: Sequence[Sequence[int]], max_tokens: int = 50,
+                           temperature: float = 0.7, ignore_eos: bool = False) -> List[List[int]]:
+        """Token ids in, token ids out; the reference's generate_batch token flow."""
+        eng = self.engine
+        B = len(prompt_ids)
+        self.prefill(prompt_ids)
+        lens = np.array([len(p) for p in prompt_ids], np.int32)
+        last = np.array([p[-1] for p in prompt_ids], np.int32)
+        total = int(lens.max()) + max_tokens
+        if total > eng.max_seq:
+            raise ValueError(f"prompt + max_tokens ({total}) exceeds max_seq {eng.max_seq}")
+        eng.tok_in[:B].copy_(torch.as_tensor(last).to(eng.device))
+        eng.pos[:B].copy_(torch.as_tensor(lens).to(eng.device))
+        gen: List[List[int]] = [[] for _ in range(B)]
+        active = np.ones(B, dtype=bool)
+        greedy = temperature == 0
+        out_dev = torch.zeros((max_tokens, B), dtype=torch.int32, device=eng.device)
+        for step in range(max_tokens):
+            if not active.any():
+                break
+            eng.step(B, logits=True, graph=self.use_graphs)
+            if greedy:
+                out_dev[step].copy_(eng.tok_out[:B])
+                nxt_dev = eng.tok_out[:B]
+                if not ignore_eos:
+                    nxt = eng.tok_out[:B].cpu().numpy()
+                    for b in np.nonzero(active)[0]:
+                        gen[b].append(int(nxt[b]))
+                        if nxt[b] == EOS_ID:
+                            active[b] = False
+            else:
+                lg = eng.logits[:B].cpu().numpy()
+                nxt = np.array([self._sample(lg[b], temperature) if active[b] else 0 for b in range(B)],
+                               np.int32)
+                for b in np.nonzero(active)[0]:
+                    gen[b].append(int(nxt[b]))
+                    if not ignore_eos and nxt[b] == EOS_ID:
+                        active[b] = False
+                nxt_dev = torch.as_tensor(nxt).to(eng.device)
+            eng.tok_in[:B].copy_(nxt_dev)
+            eng.pos[:B].add_(1)
+        if greedy and ignore_eos:
+            arr = out_dev[:max_tokens].cpu().numpy()
+            gen = [arr[:, b].tolist() for b in range(B)]
+        return gen
