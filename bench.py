@@ -1,0 +1,413 @@
+"""Benchmark: 7B-shape INT4 batched decode tokens/s on B200.
+
+Workload (the reference's headline decode configuration): a 32-layer Llama-2-7B-shaped
+random-init INT4 model (hidden 4096, 32 heads x 128, FFN 11008, vocab 32000, group-32
+scales); B independent sequences with a 512-token random prompt prefilled into the fp16
+KV cache, then greedy decode. One step = one token for each of the B sequences through
+all 32 layers, the final norm, the lm_head and the argmax. Timed steps run at positions
+515..639 (average ~577, the middle of the 513..640 decode window). Every step streams
+3.7 GB of weights plus the KV cache, so inputs are far larger than L2 (126 MB).
+
+Our arm:   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B]
+Reference: python bench.py --impl reference ...  (the reference's CPU path, restated in
+           oracle/, timed on the host cores; the Metal backend cannot run here)
+
+Under torchrun each rank runs its own B sequences (sequence data parallelism, no
+collective on the data path): scaling "weak"; the reported value is the sum over ranks
+of tokens / (max over ranks of the timed region).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG7B = {"hidden_size": 4096, "num_attention_heads": 32, "intermediate_size": 11008, "num_hidden_layers": 32,
+         "vocab_size": 32000, "rms_norm_eps": 1e-5, "max_position_embeddings": 2048}
+PROMPT = 512
+MAX_SEQ = 640
+METRIC = "7B-shape INT4 decode tok/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=125)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--extra-batches", default="1,16", help="also time these batch sizes (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=32)
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.rows.append([c.strip() for c in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------------------------------
+# model construction (random init on the device, packed with the reference rule)
+# ------------------------------------------------------------------------------------------------
+def build_model(cfg, device, max_batch, seed=1234):
+    import torch
+
+    from orchard_b200 import loader
+    from orchard_b200.model import Llama, quantize_on_device
+
+    H, F, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def packed(n, k):
+        w = (torch.randn((n, k), generator=gen, device=device, dtype=torch.float32) * 0.02).half()
+        p, s = quantize_on_device(w, device)
+        del w
+        return ("packed_dev", p, s)
+
+    ck = loader.Checkpoint(cfg)
+    for li in range(cfg["num_hidden_layers"]):
+        e = ck.layers[li]
+        for nm, shp in (("wq", (H, H)), ("wk", (H, H)), ("wv", (H, H)), ("wo", (H, H)),
+                        ("w1", (F, H)), ("w3", (F, H)), ("w2", (H, F))):
+            e[nm] = packed(*shp)
+        e["attn_norm"] = (1 + 0.1 * torch.randn(H, generator=gen, device=device)).half().float().cpu().numpy()
+        e["ffn_norm"] = (1 + 0.1 * torch.randn(H, generator=gen, device=device)).half().float().cpu().numpy()
+    ck.embed = torch.randn((V, H), generator=gen, device=device).half()
+    ck.norm = (1 + 0.1 * torch.randn(H, generator=gen, device=device)).half().float().cpu().numpy()
+    ck.lm_head = packed(V, H)
+    return Llama(checkpoint=ck, device=device, max_batch=max_batch, max_seq=MAX_SEQ)
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+def time_decode(llm, B, steps, warmup, start_pos):
+    """Device-timed decode steps (graph replays) for rows [0, B) starting at start_pos."""
+    import torch
+
+    eng = llm.engine
+    dev = eng.device
+    eng.pos[:B].fill_(start_pos)
+    for _ in range(warmup):
+        eng.step(B, logits=True)
+        eng.tok_in[:B].copy_(eng.tok_out[:B])
+        eng.pos[:B].add_(1)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        eng.step(B, logits=True)
+        eng.tok_in[:B].copy_(eng.tok_out[:B])
+        eng.pos[:B].add_(1)
+    e.record()
+    torch.cuda.synchronize(dev)
+    return s.elapsed_time(e) / 1000.0
+
+
+def kernel_profile(llm, B, pos, reps=3):
+    """Per-kernel-family device time of one eager decode step (CUDA events around each
+    launch on the launching stream), with each family's algorithmic bytes."""
+    import torch
+
+    from orchard_b200 import _lib
+    eng = llm.engine
+    cfg = eng.cfg
+    H, F, V, nh, hd = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size, cfg.num_attention_heads, cfg.head_dim
+    fam = {}
+    orig = _lib.call
+
+    def timed(name, *args):
+        st = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        rc = orig(name, *args)
+        b.record(st)
+        fam.setdefault(name, []).append((a, b, args))
+        return rc
+
+    import orchard_b200.model as M
+    M.call = timed
+    try:
+        for _ in range(reps):
+            eng.pos[:B].fill_(pos)
+            eng.step(B, logits=True, graph=False)
+        torch.cuda.synchronize()
+    finally:
+        M.call = orig
+    L = pos + 1
+    out = {}
+    for name, ev in fam.items():
+        ms = sum(a.elapsed_time(b) for a, b, _ in ev) / reps
+        n = len(ev) // reps
+        if name in ("orch_q4_qkv_rope", "orch_q4_linear_resid", "orch_q4_linear_swiglu", "orch_gemm_q4_0_ex"):
+            # weights + scales once, activations in, outputs out (fp16 in, fp16/fp32 out)
+            byts = 0
+            for _, _, args in ev[:n]:
+                if name == "orch_q4_qkv_rope":
+                    Mr, K, N = args[3], args[4], 3 * args[5]
+                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + 2 * Mr * N
+                elif name == "orch_q4_linear_swiglu":
+                    Mr, K, N = args[4], args[5], 2 * args[6]
+                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + Mr * N
+                elif name == "orch_q4_linear_resid":
+                    Mr, K, N = args[4], args[5], args[6]
+                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + 8 * Mr * N
+                else:
+                    K, N, Mr = args[6], args[7], args[8]
+                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + 4 * Mr * N
+            out["qgemm"] = out.get("qgemm", {"ms": 0.0, "bytes": 0, "launches": 0})
+            out["qgemm"]["ms"] += ms
+            out["qgemm"]["bytes"] += byts
+            out["qgemm"]["launches"] += n
+        elif name == "orch_attention_decode":
+            byts = n * (2 * B * nh * L * hd * 2 + 2 * 2 * B * nh * hd)
+            out["attention"] = {"ms": ms, "bytes": byts, "launches": n}
+        else:
+            out.setdefault("other", {"ms": 0.0, "bytes": 0, "launches": 0})
+            out["other"]["ms"] += ms
+            out["other"]["launches"] += n
+    return out
+
+
+def cpu_baseline_sample(B, target_s=15.0):
+    """The oracle's decode step on the host cores: a 2-layer 7B-shape slice at batch B with
+    577 cached positions, scaled by 16 to 32 layers (+ the lm_head once)."""
+    import oracle
+
+    cfg = dict(CFG7B, num_hidden_layers=2)
+    H, F, V = 4096, 11008, 32000
+    g = np.random.default_rng(7)
+
+    def q(n, k):  # timing does not depend on values: random codes, unit-ish scales
+        return (g.integers(0, 256, (n, k // 2), dtype=np.uint8), np.full((n, k // 32), 0.01, np.float16))
+
+    layers = [oracle.model.OracleLayer(wq=q(H, H), wk=q(H, H), wv=q(H, H), wo=q(H, H), w1=q(F, H), w3=q(F, H),
+                                       w2=q(H, F), attn_norm=np.ones(H, np.float32), ffn_norm=np.ones(H, np.float32))
+              for _ in range(2)]
+    om = oracle.model.OracleModel(cfg, layers, g.standard_normal((V, H), dtype=np.float32), np.ones(H, np.float32),
+                                  q(V, H))
+    L0 = 576
+    for li in range(2):
+        for b in range(B):
+            om.k_cache[li][b] = g.standard_normal((32, L0, 128), dtype=np.float32)
+            om.v_cache[li][b] = g.standard_normal((32, L0, 128), dtype=np.float32)
+    toks = list(range(B))
+    t_layers, t_head, n = 0.0, 0.0, 0
+    t_start = time.perf_counter()
+    while n < 1 or time.perf_counter() - t_start < target_s:
+        x = om.embed[np.asarray(toks)]
+        cos, sin = om.freqs_cos[[L0] * B], om.freqs_sin[[L0] * B]
+        t0 = time.perf_counter()
+        for li in range(2):
+            x = om.layer_forward(li, x, cos, sin, list(range(B)))
+        t1 = time.perf_counter()
+        om._lin(om.lm_head, oracle.ops.rmsnorm(x, om.norm, 1e-5))
+        t2 = time.perf_counter()
+        for li in range(2):  # keep the cache length fixed
+            for b in range(B):
+                om.k_cache[li][b] = om.k_cache[li][b][:, :L0]
+                om.v_cache[li][b] = om.v_cache[li][b][:, :L0]
+        t_layers += t1 - t0
+        t_head += t2 - t1
+        n += 1
+    step_s = (t_layers / n) * 16 + t_head / n
+    try:
+        import threadpoolctl
+        threads = max((i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()), default=1)
+    except Exception:
+        threads = os.cpu_count() or 1
+    return {"value": B / step_s, "unit": "tok/s", "cores": int(threads),
+            "kind": "port",
+            "sample": f"oracle decode step, batch {B}, 2 of 32 layers at 577 cached positions "
+                      f"(x16 extrapolated) + lm_head, {n} reps, {time.perf_counter() - t_start:.1f}s host time",
+            "step_s": step_s}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = dict(CFG7B, num_hidden_layers=args.layers)
+    B = args.batch
+    extra = [int(b) for b in args.extra_batches.split(",") if b] if (world == 1) else []
+    max_b = max([B] + extra)
+    llm = build_model(cfg, dev, max_b, seed=1234 + rank)
+    eng = llm.engine
+    g = np.random.default_rng([20261201, 4, rank])
+    prompts = g.integers(0, cfg["vocab_size"], (max_b, PROMPT)).tolist()
+    t0 = time.perf_counter()
+    llm.prefill(prompts)
+    torch.cuda.synchronize(dev)
+    prefill_s = time.perf_counter() - t0
+    start = PROMPT + 3 - args.warmup if args.warmup <= 3 else PROMPT
+    assert start + args.warmup + args.steps <= MAX_SEQ, "steps + warmup exceed the 640-position decode window"
+    # capture graphs before timing
+    eng.pos[:B].fill_(PROMPT)
+    eng.step(B, logits=True)
+    torch.cuda.synchronize(dev)
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        secs = time_decode(llm, B, args.steps, args.warmup, start)
+    t = torch.tensor([secs], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    secs_max = float(t.item())
+    tokens = B * args.steps * world
+    value = tokens / secs_max
+
+    # kernel families of one step at the mean timed position; roofline of the dominant one
+    mid = start + args.warmup + args.steps // 2
+    prof = kernel_profile(llm, B, mid)
+    dom = max(("qgemm", "attention"), key=lambda k: prof.get(k, {"ms": 0})["ms"])
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    d = prof[dom]
+    achieved = d["bytes"] / (d["ms"] / 1000.0) / 1e9
+    step_ms = secs_max / args.steps * 1000.0
+    prof_ms = sum(v["ms"] for v in prof.values())
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": "measured" if peaks else "fallback",
+                "traffic": None, "launches_per_step": d["launches"],
+                "bytes_per_step": d["bytes"], "share_of_eager_step": round(d["ms"] / prof_ms, 3),
+                "families_ms": {k: round(v["ms"], 4) for k, v in prof.items()}}
+    step_bytes = sum(v["bytes"] for v in prof.values())
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights x fp16 activations, fp32 accumulate",
+            "data": "synthetic (seeded random-init weights N(0,0.02) packed by the reference rule; random prompts)",
+            "config": {"workload": f"llama-2-7b-shape INT4 batched decode, batch {B}/GPU, prompt {PROMPT}, "
+                                   f"positions {start + args.warmup}..{start + args.warmup + args.steps - 1}",
+                       "model": "llama-2-7b-shape (32 layers, hidden 4096, 32x128 heads, FFN 11008, vocab 32000)",
+                       "global_batch": B * world, "seq_len": MAX_SEQ, "parallelism": f"dp{world} (sequence replicas)",
+                       "l2": "no flush needed: each step streams 3.7 GB of weights + KV (> 126 MB L2)"},
+            "step_hbm_bytes": step_bytes, "step_hbm_frac": round(step_bytes / (step_ms / 1000) / 1e9 / peak, 4),
+            "prefill_s": round(prefill_s, 2), "roofline": roofline,
+            "gpu_launches": eng.kernel_launches_per_step(B) * args.steps}
+    if rank == 0:
+        line["clocks"] = clk.summary()
+    # per-batch lines (N = 1 only)
+    if world == 1:
+        per = {}
+        for b in extra:
+            if b == B:
+                continue
+            eng.pos[:b].fill_(PROMPT)
+            eng.step(b, logits=True)
+            sb = time_decode(llm, b, args.steps, args.warmup, start)
+            per[str(b)] = {"tok_s": round(b * args.steps / sb, 2), "ms_per_step": round(sb / args.steps * 1000, 4)}
+        line["per_batch"] = per
+    # end to end through the public API: generate_batch_ids with per-step H2D/D2H
+    stats = {}
+    e2e_prompts = g.integers(0, cfg["vocab_size"], (B, PROMPT)).tolist()
+    llm.generate_batch_ids(e2e_prompts, max_tokens=args.steps, temperature=0, ignore_eos=True, stats=stats)
+    tt = torch.tensor([stats["decode_s"]], device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    line["e2e"] = {"value": round(B * stats["steps"] * world / float(tt.item()), 2), "unit": "tok/s",
+                   "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"],
+                   "api": "Llama.generate_batch_ids (greedy), decode phase",
+                   "prefill_s": round(stats["prefill_s"], 2)}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline_sample(B)
+        cb.pop("step_s", None)
+        line["cpu_baseline"] = cb
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    cb = cpu_baseline_sample(args.batch, target_s=max(5.0, min(60.0, 0.2 * (args.steps + args.warmup))))
+    line = {"metric": METRIC, "value": round(cb["value"], 4), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(cb["step_s"] * 1000, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 NumPy arithmetic",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"llama-2-7b-shape INT4 batched decode, batch {args.batch}, prompt {PROMPT}",
+                       "model": "llama-2-7b-shape", "global_batch": args.batch, "seq_len": MAX_SEQ,
+                       "parallelism": "host cores"},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(cb["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's compute backend is Apple Metal (unavailable on this box); its CPU path "
+                    "(orchard/model.py with the kernel arithmetic in NumPy) is the oracle port"}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)

@@ -116,7 +116,12 @@ def last_error() -> str:
 
 
 def call(name: str, *args) -> int:
-    """Calls an int-returning entry point, raising OrchardError on a nonzero status."""
+    """Calls an int-returning entry point, raising OrchardError on a nonzero status.
+
+    Tensor arguments are passed by device address and stay referenced for the duration of
+    the call; work enqueued on a stream is ordered before any later reuse of their memory
+    by the caching allocator on that stream."""
+    args = tuple(a.data_ptr() if hasattr(a, "data_ptr") else a for a in args)
     rc = getattr(lib(), name)(*args)
     if rc != 0:
         raise OrchardError(name, rc, last_error())

@@ -371,47 +371,75 @@ class Llama:
             eng.step(B, logits=False, graph=self.use_graphs)
 
     def generate_batch_ids(self, prompt_ids: Sequence[Sequence[int]], max_tokens: int = 50,
-                           temperature: float = 0.7, ignore_eos: bool = False) -> List[List[int]]:
-        """Token ids in, token ids out; the reference's generate_batch token flow."""
+                           temperature: float = 0.7, ignore_eos: bool = False,
+                           stats: Optional[dict] = None) -> List[List[int]]:
+        """Token ids in, token ids out; the reference's generate_batch token flow.
+
+        Every decode step copies that step's positions host->device (pinned) and the sampled
+        tokens device->host. With temperature 0 the next step is enqueued before the host
+        reads the previous step's tokens, so the GPU never waits on the host; a row that
+        produced EOS keeps computing (its later tokens are dropped), which leaves the other
+        rows' results unchanged. ``stats`` (optional dict) receives the prefill and decode
+        wall times, steps run and bytes copied per step."""
+        import time
+
         eng = self.engine
         B = len(prompt_ids)
-        self.prefill(prompt_ids)
         lens = np.array([len(p) for p in prompt_ids], np.int32)
-        last = np.array([p[-1] for p in prompt_ids], np.int32)
         total = int(lens.max()) + max_tokens
         if total > eng.max_seq:
             raise ValueError(f"prompt + max_tokens ({total}) exceeds max_seq {eng.max_seq}")
+        t0 = time.perf_counter()
+        self.prefill(prompt_ids)
+        torch.cuda.synchronize(eng.device)
+        t1 = time.perf_counter()
+        last = np.array([p[-1] for p in prompt_ids], np.int32)
         eng.tok_in[:B].copy_(torch.as_tensor(last).to(eng.device))
-        eng.pos[:B].copy_(torch.as_tensor(lens).to(eng.device))
+        pos_host = torch.empty((max_tokens, B), dtype=torch.int32, pin_memory=True)
+        pos_host.copy_(torch.as_tensor(lens[None, :] + np.arange(max_tokens, dtype=np.int32)[:, None]))
+        tok_host = torch.empty((max_tokens, B), dtype=torch.int32, pin_memory=True)
         gen: List[List[int]] = [[] for _ in range(B)]
         active = np.ones(B, dtype=bool)
         greedy = temperature == 0
-        out_dev = torch.zeros((max_tokens, B), dtype=torch.int32, device=eng.device)
+        stream = torch.cuda.current_stream(eng.device)
+        events: List[torch.cuda.Event] = []
+
+        def consume(step):
+            events[step].synchronize()
+            nxt = tok_host[step].numpy()
+            for b in np.nonzero(active)[0]:
+                gen[b].append(int(nxt[b]))
+                if not ignore_eos and nxt[b] == EOS_ID:
+                    active[b] = False
+
+        steps = 0
         for step in range(max_tokens):
+            if greedy and step >= 1:
+                consume(step - 1)
             if not active.any():
                 break
+            eng.pos[:B].copy_(pos_host[step], non_blocking=True)
             eng.step(B, logits=True, graph=self.use_graphs)
             if greedy:
-                out_dev[step].copy_(eng.tok_out[:B])
-                nxt_dev = eng.tok_out[:B]
-                if not ignore_eos:
-                    nxt = eng.tok_out[:B].cpu().numpy()
-                    for b in np.nonzero(active)[0]:
-                        gen[b].append(int(nxt[b]))
-                        if nxt[b] == EOS_ID:
-                            active[b] = False
+                eng.tok_in[:B].copy_(eng.tok_out[:B])
+                tok_host[step].copy_(eng.tok_out[:B], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                events.append(ev)
             else:
                 lg = eng.logits[:B].cpu().numpy()
-                nxt = np.array([self._sample(lg[b], temperature) if active[b] else 0 for b in range(B)],
-                               np.int32)
+                nxt = np.array([self._sample(lg[b], temperature) if active[b] else 0 for b in range(B)], np.int32)
                 for b in np.nonzero(active)[0]:
                     gen[b].append(int(nxt[b]))
                     if not ignore_eos and nxt[b] == EOS_ID:
                         active[b] = False
-                nxt_dev = torch.as_tensor(nxt).to(eng.device)
-            eng.tok_in[:B].copy_(nxt_dev)
-            eng.pos[:B].add_(1)
-        if greedy and ignore_eos:
-            arr = out_dev[:max_tokens].cpu().numpy()
-            gen = [arr[:, b].tolist() for b in range(B)]
+                eng.tok_in[:B].copy_(torch.as_tensor(nxt).to(eng.device))
+            steps += 1
+        if greedy and steps > 0 and len(events) == steps and active.any():
+            consume(steps - 1)
+        torch.cuda.synchronize(eng.device)
+        t2 = time.perf_counter()
+        if stats is not None:
+            stats.update(prefill_s=t1 - t0, decode_s=t2 - t1, steps=steps, batch=B,
+                         h2d_bytes_per_step=4 * B, d2h_bytes_per_step=4 * B if greedy else 4 * B * eng.cfg.vocab_size)
         return gen

@@ -69,10 +69,10 @@ def test_q4_gemm_matches_oracle(K, N, M):
     x = rng(2, M, K).standard_normal((M, K), dtype=np.float32).astype(np.float16)
     ref = x.astype(np.float32) @ q4_dense(N, K).T
     y = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    call("orch_gemm_q4_0", ptr(D(p)), ptr(D(s)), ptr(D(x)), ptr(y), K, N, M, S())
+    call("orch_gemm_q4_0", D(p), D(s), D(x), ptr(y), K, N, M, S())
     assert rel_err(y.float().cpu().numpy(), ref) <= 1e-2
     yf = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    call("orch_gemm_q4_0_ex", ptr(D(p)), ptr(D(s)), ptr(D(x.astype(np.float32))), F32, ptr(yf), F32, K, N, M, S())
+    call("orch_gemm_q4_0_ex", D(p), D(s), D(x.astype(np.float32)), F32, ptr(yf), F32, K, N, M, S())
     assert rel_err(yf.cpu().numpy(), ref) <= 1e-2
 
 
@@ -82,7 +82,7 @@ def test_gemv_kat_0x99():
     s = np.ones((1, 1), np.float16)
     x = np.ones(32, np.float16)
     y = torch.zeros(1, dtype=torch.float16, device="cuda")
-    call("orch_gemv_q4_0", ptr(D(p)), ptr(D(s)), ptr(D(x)), ptr(y), 32, 1, S())
+    call("orch_gemv_q4_0", D(p), D(s), D(x), ptr(y), 32, 1, S())
     assert float(y.item()) == 32.0
 
 
@@ -93,8 +93,8 @@ def test_q4_gemm_repeatable_and_m_independent():
     x = rng(4).standard_normal((8, K), dtype=np.float32).astype(np.float16)
     y1 = torch.empty((8, N), dtype=torch.float32, device="cuda")
     y2 = torch.empty_like(y1)
-    call("orch_gemm_q4_0_ex", ptr(D(p)), ptr(D(s)), ptr(D(x)), F16, ptr(y1), F32, K, N, 8, S())
-    call("orch_gemm_q4_0_ex", ptr(D(p)), ptr(D(s)), ptr(D(x)), F16, ptr(y2), F32, K, N, 8, S())
+    call("orch_gemm_q4_0_ex", D(p), D(s), D(x), F16, ptr(y1), F32, K, N, 8, S())
+    call("orch_gemm_q4_0_ex", D(p), D(s), D(x), F16, ptr(y2), F32, K, N, 8, S())
     assert torch.equal(y1, y2)
 
 
@@ -107,11 +107,11 @@ def test_q8_group_and_per_channel(K, N, M):
     q, s = quantizer.quantize_q8_0(w)
     ref = ops.gemv_q8_0(q, s, x.astype(np.float32))
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    call("orch_gemm_q8_0_ex", ptr(D(q)), ptr(D(s)), ptr(D(x)), F16, ptr(y), F32, K, N, M, S())
+    call("orch_gemm_q8_0_ex", D(q), D(s), D(x), F16, ptr(y), F32, K, N, M, S())
     assert rel_err(y.cpu().numpy(), ref) <= 1e-2
     qp, sp = quantizer.quantize_q8_pc(w)
     ref = ops.gemm_q8_pc(qp, sp, x.astype(np.float32))
-    call("orch_gemm_q8_pc", ptr(D(qp)), ptr(D(sp)), ptr(D(x)), F16, ptr(y), F32, K, N, M, S())
+    call("orch_gemm_q8_pc", D(qp), D(sp), D(x), F16, ptr(y), F32, K, N, M, S())
     assert rel_err(y.cpu().numpy(), ref) <= 1e-2
 
 
@@ -144,7 +144,7 @@ def test_device_quantizer_matches_reference_fixture(golden_q4):
         n, k = w.shape
         p = torch.empty((n, k // 2), dtype=torch.uint8, device="cuda")
         s = torch.empty((n, k // 32), dtype=torch.float16, device="cuda")
-        call("orch_quantize_q4_0", ptr(D(w)), F32, ptr(p), ptr(s), n, k, S())
+        call("orch_quantize_q4_0", D(w), F32, ptr(p), ptr(s), n, k, S())
         np.testing.assert_array_equal(p.cpu().numpy(), golden_q4[f"{case}_packed"])
         np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), golden_q4[f"{case}_scales"].view(np.uint16))
 
@@ -154,12 +154,12 @@ def test_device_q8_packers_bit_exact():
     w[1] = 0
     q = torch.empty((33, 128), dtype=torch.int8, device="cuda")
     s = torch.empty((33, 4), dtype=torch.float16, device="cuda")
-    call("orch_quantize_q8_0", ptr(D(w)), F32, ptr(q), ptr(s), 33, 128, S())
+    call("orch_quantize_q8_0", D(w), F32, ptr(q), ptr(s), 33, 128, S())
     hq, hs = quantizer.quantize_q8_0(w)
     np.testing.assert_array_equal(q.cpu().numpy(), hq)
     np.testing.assert_array_equal(s.cpu().numpy(), hs)
     sp = torch.empty(33, dtype=torch.float16, device="cuda")
-    call("orch_quantize_q8_pc", ptr(D(w)), F32, ptr(q), ptr(sp), 33, 128, S())
+    call("orch_quantize_q8_pc", D(w), F32, ptr(q), ptr(sp), 33, 128, S())
     hq, hs = quantizer.quantize_q8_pc(w)
     np.testing.assert_array_equal(q.cpu().numpy(), hq)
     np.testing.assert_array_equal(sp.cpu().numpy(), hs)
@@ -172,10 +172,10 @@ def test_rmsnorm(B):
     g = (1 + 0.1 * rng(10).standard_normal(4096, dtype=np.float32))
     ref = ops.rmsnorm(x, g, 1e-5)
     y = torch.empty((B, 4096), dtype=torch.float32, device="cuda")
-    call("orch_rmsnorm_ex", ptr(D(x)), F32, ptr(D(g)), F32, ptr(y), F32, 1e-5, 4096, B, S())
+    call("orch_rmsnorm_ex", D(x), F32, D(g), F32, ptr(y), F32, 1e-5, 4096, B, S())
     assert rel_err(y.cpu().numpy(), ref) <= 1e-5
     yh = torch.empty((B, 4096), dtype=torch.float16, device="cuda")
-    call("orch_rmsnorm", ptr(D(x.astype(np.float16))), ptr(D(g.astype(np.float16))), ptr(yh), 1e-5, 4096, B, S())
+    call("orch_rmsnorm", D(x.astype(np.float16)), D(g.astype(np.float16)), ptr(yh), 1e-5, 4096, B, S())
     ref16 = ops.rmsnorm(x.astype(np.float16), g.astype(np.float16), 1e-5)
     assert rel_err(yh.float().cpu().numpy(), ref16) <= 1e-3
 
@@ -187,11 +187,11 @@ def test_rope_per_row(B):
     c, s = ops.precompute_freqs_cis(128, 4096)
     ref = ops.rope(x, c[pos], s[pos])
     y = torch.empty_like(D(x))
-    call("orch_rope_ex", ptr(D(x)), F32, ptr(D(c[pos])), ptr(D(s[pos])), F32, ptr(y), F32, 128, 32, B, S())
+    call("orch_rope_ex", D(x), F32, D(c[pos]), D(s[pos]), F32, ptr(y), F32, 128, 32, B, S())
     assert rel_err(y.cpu().numpy(), ref) <= 1e-5
     yh = torch.empty((B, 32, 128), dtype=torch.float16, device="cuda")
-    call("orch_rope", ptr(D(x.astype(np.float16))), ptr(D(c[pos].astype(np.float16))),
-         ptr(D(s[pos].astype(np.float16))), ptr(yh), 128, 32, B, S())
+    call("orch_rope", D(x.astype(np.float16)), D(c[pos].astype(np.float16)),
+         D(s[pos].astype(np.float16)), ptr(yh), 128, 32, B, S())
     ref16 = ops.rope(x.astype(np.float16), c[pos].astype(np.float16), s[pos].astype(np.float16))
     assert rel_err(yh.float().cpu().numpy(), ref16) <= 1e-3
 
@@ -202,10 +202,10 @@ def test_softmax(B, L):
     x = rng(13, B, L).standard_normal((rows, L), dtype=np.float32) * 3
     ref = ops.softmax_rows(x)
     y = torch.empty((rows, L), dtype=torch.float16, device="cuda")
-    call("orch_softmax", ptr(D(x.astype(np.float16))), ptr(y), rows, L, S())
+    call("orch_softmax", D(x.astype(np.float16)), ptr(y), rows, L, S())
     np.testing.assert_allclose(y.float().cpu().numpy(), ops.softmax_rows(x.astype(np.float16)), atol=1e-3)
     yf = torch.empty((rows, L), dtype=torch.float32, device="cuda")
-    call("orch_softmax_ex", ptr(D(x)), F32, ptr(yf), F32, rows, L, S())
+    call("orch_softmax_ex", D(x), F32, ptr(yf), F32, rows, L, S())
     np.testing.assert_allclose(yf.cpu().numpy(), ref, atol=1e-6, rtol=1e-4)
 
 
@@ -230,17 +230,17 @@ def test_full_test_kats():
     a = rng(16).random(1024).astype(np.float16)
     b = rng(17).random(1024).astype(np.float16)
     c = torch.empty(1024, dtype=torch.float16, device="cuda")
-    call("orch_add", ptr(D(a)), ptr(D(b)), ptr(c), 1024, S())
+    call("orch_add", D(a), D(b), ptr(c), 1024, S())
     np.testing.assert_allclose(c.cpu().numpy(), a + b, atol=1e-3)
-    call("orch_mul", ptr(D(a)), ptr(D(b)), ptr(c), 1024, S())
+    call("orch_mul", D(a), D(b), ptr(c), 1024, S())
     np.testing.assert_allclose(c.cpu().numpy(), a * b, atol=1e-3)
-    call("orch_silu", ptr(D(a)), ptr(c), 1024, S())
+    call("orch_silu", D(a), ptr(c), 1024, S())
     af = a.astype(np.float32)
     np.testing.assert_allclose(c.cpu().numpy(), (af / (1 + np.exp(-af))).astype(np.float16), atol=1e-3)
     ids = np.array([1, 50, 99, 0], np.int32)
     table = rng(18).random((100, 64)).astype(np.float16)
     out = torch.empty((4, 64), dtype=torch.float16, device="cuda")
-    call("orch_embedding", ptr(D(ids)), ptr(D(table)), ptr(out), 4, 64, 100, S())
+    call("orch_embedding", D(ids), D(table), ptr(out), 4, 64, 100, S())
     np.testing.assert_array_equal(out.cpu().numpy(), table[ids])
 
 
@@ -250,7 +250,7 @@ def test_embedding_rejects_out_of_range_ids():
     out = torch.full((3, 8), 7.0, dtype=torch.float16, device="cuda")
     flags = _lib.C.c_uint32(0)
     call("orch_device_check", _lib.C.byref(flags), None)
-    call("orch_embedding", ptr(D(ids)), ptr(D(table)), ptr(out), 3, 8, 100, S())
+    call("orch_embedding", D(ids), D(table), ptr(out), 3, 8, 100, S())
     call("orch_device_check", _lib.C.byref(flags), None)
     assert flags.value & 4
     o = out.cpu().numpy()
@@ -263,10 +263,10 @@ def test_dense_matmuls(M, N, K):
     a = rng(20, M, K).random((M, K), dtype=np.float32)
     b = rng(21, K, N).random((K, N), dtype=np.float32)
     c = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    call("orch_matmul", ptr(D(a)), ptr(D(b)), ptr(c), M, N, K, S())
+    call("orch_matmul", D(a), D(b), ptr(c), M, N, K, S())
     np.testing.assert_allclose(c.cpu().numpy(), ops.matmul(a, b), rtol=1e-5, atol=1e-4 * K / 16)
     ch = torch.empty((M, N), dtype=torch.float16, device="cuda")
-    call("orch_matmul_simd", ptr(D(a.astype(np.float16))), ptr(D(b.astype(np.float16))), ptr(ch), M, N, K, S())
+    call("orch_matmul_simd", D(a.astype(np.float16)), D(b.astype(np.float16)), ptr(ch), M, N, K, S())
     ref = ops.matmul(a.astype(np.float16), b.astype(np.float16))
     assert rel_err(ch.float().cpu().numpy(), ref) <= 2e-3
 
@@ -276,7 +276,7 @@ def test_argmax_first_max():
     lg[2, 7] = lg[2, 9] = 100.0
     lg[4, :] = 1.0
     out = torch.empty(5, dtype=torch.int32, device="cuda")
-    call("orch_argmax_rows", ptr(D(lg)), 5, 32000, ptr(out), S())
+    call("orch_argmax_rows", D(lg), 5, 32000, ptr(out), S())
     np.testing.assert_array_equal(out.cpu().numpy(), np.argmax(lg, axis=1))
 
 
@@ -294,7 +294,7 @@ def test_attention_decode(M, L, hd):
     ws_bytes = _lib.lib().orch_attention_workspace_bytes(M, nh, hd, max_seq)
     ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device="cuda")
     out = torch.empty((M, nh * hd), dtype=torch.float16, device="cuda")
-    call("orch_attention_decode", ptr(D(q)), ptr(D(kc)), ptr(D(vc)), ptr(D(pos)), ptr(D(slots)), ptr(out),
+    call("orch_attention_decode", D(q), D(kc), D(vc), D(pos), D(slots), ptr(out),
          M, nh, hd, max_seq, ptr(ws), ws_bytes, S())
     o = out.float().cpu().numpy()
     for m in range(M):
