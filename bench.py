@@ -117,7 +117,7 @@ def build_model(cfg, device, max_batch, seed=1234):
         w = (torch.randn((n, k), generator=gen, device=device, dtype=torch.float32) * 0.02).half()
         p, s = quantize_on_device(w, device)
         del w
-        return ("packed_dev", p, s)
+        return ("packed", p, s)
 
     ck = loader.Checkpoint(cfg)
     for li in range(cfg["num_hidden_layers"]):

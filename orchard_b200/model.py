@@ -95,11 +95,24 @@ def quantize_on_device(w, device) -> tuple:
     return packed, scales
 
 
+def _as_device(a, device, np_dtype=None) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        return a.to(device).contiguous()
+    a = np.ascontiguousarray(a)
+    if np_dtype is not None:
+        a = a.view(np_dtype) if a.dtype.itemsize == np.dtype(np_dtype).itemsize else a.astype(np_dtype)
+    return torch.as_tensor(a).to(device)
+
+
 def _packed_on_device(entry, device) -> tuple:
+    """A checkpoint entry -> (packed, scales) device tensors. Entries are
+    ("packed", packed, scales) -- host arrays or device tensors -- or ("dense", weight)."""
     if entry[0] == "packed":
-        p = torch.as_tensor(np.ascontiguousarray(entry[1]).view(np.uint8)).to(device)
-        s = torch.as_tensor(np.ascontiguousarray(entry[2]).astype(np.float16)).to(device)
-        return p, s
+        p = _as_device(entry[1], device, np.uint8)
+        s = _as_device(entry[2], device, np.float16)
+        if p.dtype != torch.uint8:
+            p = p.view(torch.uint8)
+        return p, s.to(torch.float16)
     return quantize_on_device(entry[1], device)
 
 
@@ -176,8 +189,10 @@ class DecodeEngine:
         self.max_pos = max(self.max_seq, cfg.max_position_embeddings)
         dev = self.device
         self.layers = [DeviceLayer(e, cfg, dev) for e in ck.layers]
-        emb = np.asarray(ck.embed)
-        self.embed = torch.as_tensor(emb if emb.dtype in (np.float16, np.float32) else emb.astype(np.float32)).to(dev)
+        emb = ck.embed if isinstance(ck.embed, torch.Tensor) else torch.as_tensor(np.asarray(ck.embed))
+        if emb.dtype not in (torch.float16, torch.float32):
+            emb = emb.float()
+        self.embed = emb.to(dev).contiguous()
         self.norm = torch.as_tensor(np.asarray(ck.norm, np.float32)).to(dev)
         self.lm_w, self.lm_s = _packed_on_device(ck.lm_head, dev)
         cos, sin = precompute_freqs_cis(cfg.head_dim, self.max_pos, cfg.rope_theta)
@@ -199,7 +214,7 @@ class DecodeEngine:
         self.slots = torch.arange(B, dtype=torch.int32, device=dev)
         self.lora_r = 0
         self.lora_t = torch.zeros((B, 3 * 64), dtype=torch.float32, device=dev)
-        ws = _lib.lib().orch_attention_workspace_bytes(B, nh, hd, self.max_seq)
+        ws = max(_lib.lib().orch_attention_workspace_bytes(m, nh, hd, self.max_seq) for m in range(1, B + 1))
         self.attn_ws = torch.zeros(max(ws, 16) // 4 + 1, dtype=torch.float32, device=dev)
         self.attn_ws_bytes = ws
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
