@@ -174,6 +174,10 @@ int orch_attention_decode(const void* q, const void* k_cache, const void* v_cach
                           const int32_t* pos, const int32_t* slots, void* out, uint32_t M,
                           uint32_t num_heads, uint32_t head_dim, uint32_t max_seq,
                           void* workspace, size_t workspace_bytes, void* stream);
+/* INT4 GEMMs with fp16 activations and at least `m` rows run on the tcgen05 tensor-core
+ * kernel (TMEM accumulators, TMA-fed activations); fewer rows use the mma.sync decode
+ * kernel. 0 disables the tensor-core kernel. Default 17 (ORCHARD_TC_MIN_M overrides). */
+int orch_set_tc_min_m(uint32_t m);
 /* Row argmax of fp32 logits [M, V] (first index of the maximum, as np.argmax;
  * orchard/model.py:244-246). */
 int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, void* stream);

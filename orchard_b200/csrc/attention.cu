@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   __shared__ float sc[kAttnChunk];
   __shared__ float red[32];
   __shared__ float accs[kAttnThreads / 32][HD];
+  pdl_trigger();
+  pdl_wait();
 
   const int mh = blockIdx.x;
   const int m = mh / a.nh, h = mh - m * a.nh;
@@ -152,6 +154,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
 
 template <int HD>
 __global__ void attn_combine_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int mh = blockIdx.x;
   const int m = mh / a.nh, h = mh - m * a.nh;
   const int p = a.pos[m];
@@ -183,8 +187,9 @@ static int attn_splits(int M, int nh, int max_seq) {
 template <int HD>
 static int attn_launch(AttnArgs a, cudaStream_t st) {
   dim3 grid(a.M * a.nh, a.S);
-  attn_decode_kernel<HD><<<grid, kAttnThreads, 0, st>>>(a);
-  if (a.S > 1) attn_combine_kernel<HD><<<a.M * a.nh, HD, 0, st>>>(a);
+  const dim3 none(0, 0, 0);
+  ORCH_CUDA(launch_k(attn_decode_kernel<HD>, grid, dim3(kAttnThreads), 0, st, none, a));
+  if (a.S > 1) ORCH_CUDA(launch_k(attn_combine_kernel<HD>, dim3(a.M * a.nh), dim3(HD), 0, st, none, a));
   return check_launch("attention_decode");
 }
 
@@ -192,6 +197,8 @@ static int attn_launch(AttnArgs a, cudaStream_t st) {
 template <typename TI, typename TO>
 __global__ void softmax_rows_kernel(const TI* in, TO* out, int cols) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const TI* r = in + (size_t)blockIdx.x * cols;
   TO* o = out + (size_t)blockIdx.x * cols;
   float mx = -INFINITY;
@@ -208,6 +215,8 @@ __global__ void softmax_rows_kernel(const TI* in, TO* out, int cols) {
 __global__ void argmax_rows_kernel(const float* logits, int V, int* out) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_trigger();
+  pdl_wait();
   const float* r = logits + (size_t)blockIdx.x * V;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -301,13 +310,13 @@ extern "C" int orch_softmax_ex(const void* in, int in_dt, void* out, int out_dt,
   cudaStream_t st = as_stream(stream);
   const int th = cols >= 1024 ? 1024 : cols >= 256 ? 256 : 128;
   if (in_dt == ORCH_F16 && out_dt == ORCH_F16)
-    softmax_rows_kernel<__half, __half><<<rows, th, 0, st>>>((const __half*)in, (__half*)out, cols);
+    ORCH_CUDA(launch_k(softmax_rows_kernel<__half, __half>, dim3(rows), dim3(th), 0, st, dim3(0, 0, 0), (const __half*)in, (__half*)out, cols));
   else if (in_dt == ORCH_F32 && out_dt == ORCH_F32)
-    softmax_rows_kernel<float, float><<<rows, th, 0, st>>>((const float*)in, (float*)out, cols);
+    ORCH_CUDA(launch_k(softmax_rows_kernel<float, float>, dim3(rows), dim3(th), 0, st, dim3(0, 0, 0), (const float*)in, (float*)out, cols));
   else if (in_dt == ORCH_F16 && out_dt == ORCH_F32)
-    softmax_rows_kernel<__half, float><<<rows, th, 0, st>>>((const __half*)in, (float*)out, cols);
+    ORCH_CUDA(launch_k(softmax_rows_kernel<__half, float>, dim3(rows), dim3(th), 0, st, dim3(0, 0, 0), (const __half*)in, (float*)out, cols));
   else if (in_dt == ORCH_F32 && out_dt == ORCH_F16)
-    softmax_rows_kernel<float, __half><<<rows, th, 0, st>>>((const float*)in, (__half*)out, cols);
+    ORCH_CUDA(launch_k(softmax_rows_kernel<float, __half>, dim3(rows), dim3(th), 0, st, dim3(0, 0, 0), (const float*)in, (__half*)out, cols));
   else
     return fail(ORCH_ERR_INVALID, "softmax: bad dtype");
   return check_launch("softmax");
@@ -320,6 +329,7 @@ extern "C" int orch_softmax(const void* in, void* out, uint32_t rows, uint32_t c
 extern "C" int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, void* stream) {
   if (M == 0) return ORCH_OK;
   ORCH_REQUIRE(logits && out && V > 0, "argmax_rows: bad arguments");
-  argmax_rows_kernel<<<M, 1024, 0, as_stream(stream)>>>(logits, (int)V, out);
+  ORCH_CUDA(launch_k(argmax_rows_kernel, dim3(M), dim3(1024), 0, as_stream(stream), dim3(0, 0, 0), logits,
+                     (int)V, (int*)out));
   return check_launch("argmax_rows");
 }

@@ -3,6 +3,7 @@
 #include <sys/stat.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -29,6 +30,13 @@ int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_status(e, what);
   return ORCH_OK;
+}
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ORCHARD_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 int device_index() {
   int d = 0;

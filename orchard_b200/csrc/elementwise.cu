@@ -14,6 +14,8 @@ namespace orch {
 template <typename TI, typename TW, typename TO>
 __global__ void rmsnorm_kernel(const TI* in, const TW* w, TO* out, float eps, int N) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
   const TI* r = in + (size_t)blockIdx.x * N;
   TO* o = out + (size_t)blockIdx.x * N;
   float ss = 0.f;
@@ -30,6 +32,8 @@ __global__ void rmsnorm_kernel(const TI* in, const TW* w, TO* out, float eps, in
 template <typename TI, typename TT, typename TO>
 __global__ void rope_kernel(const TI* in, const TT* cs, const TT* sn, TO* out, int hd, int heads,
                             int rows) {
+  pdl_trigger();
+  pdl_wait();
   const int half = hd >> 1;
   const size_t total = (size_t)rows * heads * half;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -49,6 +53,8 @@ __global__ void rope_kernel(const TI* in, const TT* cs, const TT* sn, TO* out, i
 // ---- elementwise -------------------------------------------------------------------------
 template <typename T, int OP>
 __global__ void binary_kernel(const T* a, const T* b, T* c, size_t n) {
+  pdl_trigger();
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float x = to_f32(a[i]), y = to_f32(b[i]);
     c[i] = from_f32<T>(OP == 0 ? x + y : x * y);
@@ -57,6 +63,8 @@ __global__ void binary_kernel(const T* a, const T* b, T* c, size_t n) {
 
 template <typename T>
 __global__ void silu_kernel(const T* in, T* out, size_t n) {
+  pdl_trigger();
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float x = to_f32(in[i]);
     out[i] = from_f32<T>(x / (1.0f + expf(-x)));
@@ -67,6 +75,8 @@ __global__ void silu_kernel(const T* in, T* out, size_t n) {
 template <typename TW, typename TO>
 __global__ void embedding_kernel(const int* ids, const TW* w, TO* out, int tokens, int hd, int vocab,
                                  uint32_t* check) {
+  pdl_trigger();
+  pdl_wait();
   const size_t total = (size_t)tokens * hd;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / hd), d = (int)(i % hd);
@@ -85,6 +95,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) matmul_kernel(const T* A, const T* B, T* C, int M, int N, int K) {
   __shared__ float As[16][64 + 1];
   __shared__ float Bs[16][64 + 1];
+  pdl_trigger();
+  pdl_wait();
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
   float acc[4][4] = {};
@@ -141,8 +153,8 @@ extern "C" int orch_rmsnorm_ex(const void* in, int in_dt, const void* weight, in
   cudaStream_t st = as_stream(stream);
   const int th = N >= 1024 ? 256 : 128;
 #define RMS_CASE(TI, TW, TO)                                                                   \
-  rmsnorm_kernel<TI, TW, TO><<<count, th, 0, st>>>((const TI*)in, (const TW*)weight, (TO*)out, \
-                                                   eps, (int)N)
+  ORCH_CUDA(launch_k(rmsnorm_kernel<TI, TW, TO>, dim3(count), dim3(th), 0, st, dim3(0, 0, 0), (const TI*)in, \
+                     (const TW*)weight, (TO*)out, eps, (int)N))
   const int key = in_dt * 4 + w_dt * 2 + out_dt;
   switch (key) {
     case 0: RMS_CASE(float, float, float); break;
@@ -174,8 +186,8 @@ extern "C" int orch_rope_ex(const void* in, int in_dt, const void* cs, const voi
   const size_t n = (size_t)seq_len * num_heads * (head_dim / 2);
   const int g = grid_for(n, 256);
 #define ROPE_CASE(TI, TT, TO)                                                                 \
-  rope_kernel<TI, TT, TO><<<g, 256, 0, st>>>((const TI*)in, (const TT*)cs, (const TT*)sn, (TO*)out, \
-                                             (int)head_dim, (int)num_heads, (int)seq_len)
+  ORCH_CUDA(launch_k(rope_kernel<TI, TT, TO>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const TI*)in, \
+                     (const TT*)cs, (const TT*)sn, (TO*)out, (int)head_dim, (int)num_heads, (int)seq_len))
   const int key = in_dt * 4 + tab_dt * 2 + out_dt;
   switch (key) {
     case 0: ROPE_CASE(float, float, float); break;
@@ -205,11 +217,11 @@ extern "C" int orch_binary_ex(int op, const void* a, const void* b, void* c, int
   cudaStream_t st = as_stream(stream);
   const int g = grid_for(size, 256);
   if (dt == ORCH_F16) {
-    if (op == 0) binary_kernel<__half, 0><<<g, 256, 0, st>>>((const __half*)a, (const __half*)b, (__half*)c, size);
-    else binary_kernel<__half, 1><<<g, 256, 0, st>>>((const __half*)a, (const __half*)b, (__half*)c, size);
+    if (op == 0) ORCH_CUDA(launch_k(binary_kernel<__half, 0>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const __half*)a, (const __half*)b, (__half*)c, (size_t)size));
+    else ORCH_CUDA(launch_k(binary_kernel<__half, 1>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const __half*)a, (const __half*)b, (__half*)c, (size_t)size));
   } else {
-    if (op == 0) binary_kernel<float, 0><<<g, 256, 0, st>>>((const float*)a, (const float*)b, (float*)c, size);
-    else binary_kernel<float, 1><<<g, 256, 0, st>>>((const float*)a, (const float*)b, (float*)c, size);
+    if (op == 0) ORCH_CUDA(launch_k(binary_kernel<float, 0>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const float*)a, (const float*)b, (float*)c, (size_t)size));
+    else ORCH_CUDA(launch_k(binary_kernel<float, 1>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const float*)a, (const float*)b, (float*)c, (size_t)size));
   }
   return check_launch("binary");
 }
@@ -227,8 +239,8 @@ extern "C" int orch_silu_ex(const void* in, void* out, int dt, uint32_t size, vo
   ORCH_REQUIRE(DT_OK(dt), "silu: bad dtype");
   cudaStream_t st = as_stream(stream);
   const int g = grid_for(size, 256);
-  if (dt == ORCH_F16) silu_kernel<__half><<<g, 256, 0, st>>>((const __half*)in, (__half*)out, size);
-  else silu_kernel<float><<<g, 256, 0, st>>>((const float*)in, (float*)out, size);
+  if (dt == ORCH_F16) ORCH_CUDA(launch_k(silu_kernel<__half>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const __half*)in, (__half*)out, (size_t)size));
+  else ORCH_CUDA(launch_k(silu_kernel<float>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const float*)in, (float*)out, (size_t)size));
   return check_launch("silu");
 }
 extern "C" int orch_silu(const void* in, void* out, uint32_t size, void* stream) {
@@ -247,13 +259,13 @@ extern "C" int orch_embedding_ex(const void* ids, const void* weights, int w_dt,
   uint32_t* chk = device_check_word();
   const int* id = (const int*)ids;
   if (w_dt == ORCH_F16 && out_dt == ORCH_F16)
-    embedding_kernel<__half, __half><<<g, 256, 0, st>>>(id, (const __half*)weights, (__half*)out, num_tokens, hidden_dim, vocab, chk);
+    ORCH_CUDA(launch_k(embedding_kernel<__half, __half>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), id, (const __half*)weights, (__half*)out, (int)num_tokens, (int)hidden_dim, (int)vocab, chk));
   else if (w_dt == ORCH_F16)
-    embedding_kernel<__half, float><<<g, 256, 0, st>>>(id, (const __half*)weights, (float*)out, num_tokens, hidden_dim, vocab, chk);
+    ORCH_CUDA(launch_k(embedding_kernel<__half, float>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), id, (const __half*)weights, (float*)out, (int)num_tokens, (int)hidden_dim, (int)vocab, chk));
   else if (out_dt == ORCH_F16)
-    embedding_kernel<float, __half><<<g, 256, 0, st>>>(id, (const float*)weights, (__half*)out, num_tokens, hidden_dim, vocab, chk);
+    ORCH_CUDA(launch_k(embedding_kernel<float, __half>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), id, (const float*)weights, (__half*)out, (int)num_tokens, (int)hidden_dim, (int)vocab, chk));
   else
-    embedding_kernel<float, float><<<g, 256, 0, st>>>(id, (const float*)weights, (float*)out, num_tokens, hidden_dim, vocab, chk);
+    ORCH_CUDA(launch_k(embedding_kernel<float, float>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), id, (const float*)weights, (float*)out, (int)num_tokens, (int)hidden_dim, (int)vocab, chk));
   return check_launch("embedding");
 }
 
@@ -272,7 +284,8 @@ extern "C" int orch_matmul(const float* a, const float* b, float* c, uint32_t M,
   if (M == 0 || N == 0) return ORCH_OK;
   ORCH_REQUIRE(a && b && c, "matmul: null pointer");
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  matmul_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(a, b, c, (int)M, (int)N, (int)K);
+  ORCH_CUDA(launch_k(matmul_kernel<float>, grid, dim3(256), 0, as_stream(stream), dim3(0, 0, 0), a, b, c, (int)M,
+                     (int)N, (int)K));
   return check_launch("matmul");
 }
 
@@ -281,8 +294,8 @@ extern "C" int orch_matmul_simd(const void* a, const void* b, void* c, uint32_t 
   if (M == 0 || N == 0) return ORCH_OK;
   ORCH_REQUIRE(a && b && c, "matmul_simd: null pointer");
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  matmul_kernel<__half><<<grid, 256, 0, as_stream(stream)>>>((const __half*)a, (const __half*)b, (__half*)c,
-                                                            (int)M, (int)N, (int)K);
+  ORCH_CUDA(launch_k(matmul_kernel<__half>, grid, dim3(256), 0, as_stream(stream), dim3(0, 0, 0), (const __half*)a,
+                     (const __half*)b, (__half*)c, (int)M, (int)N, (int)K));
   return check_launch("matmul_simd");
 }
 
@@ -290,6 +303,8 @@ extern "C" int orch_matmul_simd(const void* a, const void* b, void* c, uint32_t 
 namespace orch {
 __global__ void __launch_bounds__(256) lora_xa_kernel(const __half* x, const float* A, float* t, int K, int R) {
   __shared__ float part[8][33];
+  pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const __half* xr = x + (size_t)m * K;
@@ -315,6 +330,7 @@ extern "C" int orch_lora_xa(const void* x, const float* a, float* t, uint32_t M,
                             void* stream) {
   if (M == 0 || R == 0) return ORCH_OK;
   ORCH_REQUIRE(x && a && t && K > 0, "lora_xa: bad arguments");
-  orch::lora_xa_kernel<<<M, 256, 0, as_stream(stream)>>>((const __half*)x, a, t, (int)K, (int)R);
+  ORCH_CUDA(orch::launch_k(orch::lora_xa_kernel, dim3(M), dim3(256), 0, as_stream(stream), dim3(0, 0, 0),
+                           (const __half*)x, a, t, (int)K, (int)R));
   return check_launch("lora_xa");
 }

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/orchard_b200.h"
 
@@ -23,6 +24,35 @@ int device_index();
 uint32_t* device_check_word();  // per-device flag word, set by kernels' own bounds checks
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+bool pdl_enabled();  // ORCHARD_PDL=0 in the environment turns programmatic launch off
+
+// Launch with programmatic stream serialization (and an optional cluster shape).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     dim3 cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster.x > 0) {  // dim3(0, 0, 0): no cluster
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 #define ORCH_REQUIRE(cond, msg)                                  \
   do {                                                           \
@@ -65,7 +95,7 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 // D += A(16x16 f16, row) * B(16x8 f16, col), fp32 accumulators.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -80,6 +110,14 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p) {
                : "l"(p));
   return r;
 }
+
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization
+// attribute may start while the previous kernel on the stream is still running; it must
+// call pdl_wait() before reading that kernel's output or writing anything the previous
+// kernel reads. pdl_trigger() lets the next kernel start launching. Both are no-ops for a
+// kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -26,7 +26,7 @@
 
 #include "qgemm.cuh"
 
-namespace cg = cooperative_groups;
+
 
 namespace orch {
 
@@ -97,27 +97,13 @@ __device__ __forceinline__ uint32_t dq8(uint32_t wx, uint32_t sel) {
   return h2_bits(__hsub2(v, bits_h2(0x64806480u)));
 }
 
-// LoRA term of output column `col` of region `reg` (R regions of width `width`):
-// sum_q t[n, reg, q] * B[reg, q, col].
-template <int R>
-__device__ __forceinline__ float lora_delta_r(const QArgs& a, int n, int reg, int col, int width) {
-  const float* t = a.lora_t + ((size_t)n * R + reg) * a.lora_r;
-  const float* bm = a.lora_b + (size_t)reg * a.lora_r * width + col;
-  float v = 0.f;
-  for (int q = 0; q < a.lora_r; ++q) v = fmaf(t[q], bm[(size_t)q * width], v);
-  return v;
-}
-
 template <int WF, int NT, int MT, int EPI>
 __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
-  auto lora_delta = [](const QArgs& aa, int n, int reg, int col, int width) {
-    constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
-    return lora_delta_r<R>(aa, n, reg, col, width);
-  };
   extern __shared__ __align__(16) uint4 sm[];
   constexpr int ROWS = kWarps * 16 * MT;
   constexpr int P = WCfg<WF>::kPieces;
-  constexpr int U = (MT * P >= 4) ? 1 : (MT * P == 2 ? 2 : 4);
+  // chunks per load batch; two batches are in flight (ping-pong registers)
+  constexpr int U = (NT >= 8) ? 1 : ((MT * P >= 4) ? 1 : (MT * P == 2 ? 2 : 4));
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
@@ -126,8 +112,10 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
   const int nunits = (c1 - c0) * 16;
   const int RS = nunits + 2;
 
-  stage_x<WF>(sm, a, c0 * 128, nunits, RS);
-  __syncthreads();
+  const int R0 = blockIdx.x * ROWS;
+  const int rowbase = R0 + warp * 16 * MT;
+  const int G = a.K >> 5;  // 32-k groups
+  const size_t rowbytes = (WF == W_Q4) ? (size_t)(a.K >> 1) : (size_t)a.K;
 
   float acc[MT][NT][4];
 #pragma unroll
@@ -137,14 +125,11 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
 
-  const int R0 = blockIdx.x * ROWS;
-  const int rowbase = R0 + warp * 16 * MT;
-  const int G = a.K >> 5;  // 32-k groups
-  const size_t rowbytes = (WF == W_Q4) ? (size_t)(a.K >> 1) : (size_t)a.K;
+  uint4 wa[U][MT][2][P], wb[U][MT][2][P];
+  uint32_t sa[U][MT][2], sb[U][MT][2];
 
-  for (int ch = c0; ch < c1; ch += U) {
-    uint4 wv[U][MT][2][P];
-    uint32_t sc[U][MT][2];
+  // Weight stream of chunks [ch, ch + U) into registers (independent of the activations).
+  auto load = [&](int ch, uint4 (&wv)[U][MT][2][P], uint32_t (&sc)[U][MT][2]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int grp = (ch + u) * 4 + c;
@@ -170,6 +155,9 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
         }
       }
     }
+  };
+
+  auto compute = [&](int ch, const uint4 (&wv)[U][MT][2][P], const uint32_t (&sc)[U][MT][2]) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (ch + u >= c1) break;
@@ -229,6 +217,21 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
         }
       }
     }
+  };
+
+  // Prologue: the first weight batch is requested before waiting on the previous kernel,
+  // so it streams while that kernel finishes.
+  load(c0, wa, sa);
+  pdl_trigger();
+  pdl_wait();
+  stage_x<WF>(sm, a, c0 * 128, nunits, RS);
+  __syncthreads();
+
+  for (int ch = c0; ch < c1; ch += 2 * U) {
+    load(ch + U, wb, sb);
+    compute(ch, wa, sa);
+    load(ch + 2 * U, wa, sa);
+    compute(ch + U, wb, sb);
   }
 
   // ---- partial tile -> shared memory: red[n][row] (fp32) --------------------------------
@@ -251,94 +254,7 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
       }
     }
   }
-  cg::cluster_group cl = cg::this_cluster();
-  cl.sync();
-
-  auto total = [&](int n, int rl) {
-    float v = 0.f;
-    for (int r = 0; r < KS; ++r) v += cl.map_shared_rank(red, r)[n * LDR + rl];
-    return v;
-  };
-
-  if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    const int items = a.M * ROWS;
-    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
-    for (int i = i0 + threadIdx.x; i < i1; i += kThreads) {
-      const int n = i / ROWS, rl = i - n * ROWS;
-      const int row = R0 + rl;
-      if (row >= a.N) continue;
-      float v = total(n, rl);
-      if (WF == W_Q8PC) v *= __half2float(a.s[row]);
-      if (a.lora_t != nullptr) v += lora_delta(a, n, 0, row, a.N);
-      const size_t o = (size_t)n * a.ldo + row;
-      if (EPI == EPI_RESID) {
-        float* y = static_cast<float*>(a.out);
-        y[o] = y[o] + v;
-      } else if (a.out_f32) {
-        static_cast<float*>(a.out)[o] = v;
-      } else {
-        static_cast<__half*>(a.out)[o] = __float2half_rn(v);
-      }
-    }
-  } else if (EPI == EPI_SWIGLU) {
-    const int F = a.N >> 1;
-    const int items = a.M * (ROWS / 2);
-    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
-    for (int i = i0 + threadIdx.x; i < i1; i += kThreads) {
-      const int n = i / (ROWS / 2), jj = i - n * (ROWS / 2);
-      const int b = jj >> 4, ii = jj & 15;
-      const int j = (R0 >> 1) + 16 * b + ii;
-      if (j >= F) continue;
-      float gt = total(n, 32 * b + ii);
-      float up = total(n, 32 * b + 16 + ii);
-      if (a.lora_t != nullptr) {
-        gt += lora_delta(a, n, 0, j, F);
-        up += lora_delta(a, n, 1, j, F);
-      }
-      const float si = gt / (1.0f + expf(-gt));
-      static_cast<__half*>(a.out)[(size_t)n * F + j] = __float2half_rn(si * up);
-    }
-  } else {  // EPI_QKV
-    const int items = a.M * (ROWS / 2);
-    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
-    const int half_hd = a.hd >> 1;
-    for (int i = i0 + threadIdx.x; i < i1; i += kThreads) {
-      const int n = i / (ROWS / 2), pr = i - n * (ROWS / 2);
-      const int row = R0 + 2 * pr;
-      if (row >= a.N) continue;
-      const int region = row / a.H;
-      const int rr = row - region * a.H;
-      const int head = rr / a.hd, d = rr - head * a.hd;
-      float v0 = total(n, 2 * pr), v1 = total(n, 2 * pr + 1);
-      if (a.lora_t != nullptr) {
-        v0 += lora_delta(a, n, region, rr, a.H);
-        v1 += lora_delta(a, n, region, rr + 1, a.H);
-      }
-      const int p = a.pos[n];
-      if (p < 0 || p >= a.max_seq || p >= a.max_pos) {
-        atomicOr(a.check, 1u);
-        continue;
-      }
-      if (region < 2) {
-        const float cs = a.cos_tab[(size_t)p * half_hd + (d >> 1)];
-        const float sn = a.sin_tab[(size_t)p * half_hd + (d >> 1)];
-        const float r0 = v0 * cs - v1 * sn;
-        const float r1 = v0 * sn + v1 * cs;
-        v0 = r0;
-        v1 = r1;
-      }
-      const __half2 hv = __floats2half2_rn(v0, v1);
-      if (region == 0) {
-        *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
-      } else {
-        const int slot = a.slots ? a.slots[n] : n;
-        __half* cache = region == 1 ? a.kc : a.vc;
-        const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
-        *reinterpret_cast<__half2*>(cache + off) = hv;
-      }
-    }
-  }
-  cl.sync();
+  qgemm_epilogue<WF, EPI, ROWS>(a, red, KS, ks, R0);
 }
 
 // ------------------------------------------------------------------------------------
@@ -346,7 +262,8 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
 // ------------------------------------------------------------------------------------
 namespace {
 
-constexpr int kSmemBudget = 110 * 1024;
+constexpr int kSmemBudget = 110 * 1024;  // two CTAs per SM
+constexpr int kSmemMax = 200 * 1024;     // one CTA per SM
 
 template <int WF, int NT, int MT, int EPI>
 int launch_cfg(QArgs a, int KS, size_t smem, cudaStream_t st) {
@@ -354,23 +271,12 @@ int launch_cfg(QArgs a, int KS, size_t smem, cudaStream_t st) {
   const int dev = device_index();
   auto kern = qgemm_kernel<WF, NT, MT, EPI>;
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    ORCH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    ORCH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024));
     attr_done[dev] = true;
   }
   constexpr int ROWS = kWarps * 16 * MT;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + ROWS - 1) / ROWS, KS, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = KS;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  ORCH_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+  ORCH_CUDA(launch_k(kern, dim3((a.N + ROWS - 1) / ROWS, KS, 1), dim3(kThreads, 1, 1), smem, st,
+                     dim3(1, KS, 1), a));
   return ORCH_OK;
 }
 
@@ -393,6 +299,10 @@ template <int WF, int EPI>
 int qgemm_run(QArgs a, cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0) return ORCH_OK;
   if (a.K <= 0 || (a.K % 32) != 0) return fail(ORCH_ERR_UNSUPPORTED, "K must be a positive multiple of 32");
+  if (WF == W_Q4 && !a.x_f32 && tc_min_m() > 0 && a.M >= (int)tc_min_m()) {
+    const int rc = tc_qgemm_run<EPI>(a, st);
+    if (rc != ORCH_ERR_UNSUPPORTED) return rc;
+  }
   a.nchunk = (a.K + 127) / 128;
   a.check = device_check_word();
   const int total_M = a.M;
@@ -410,8 +320,9 @@ int qgemm_run(QArgs a, cudaStream_t st) {
       return (size_t)m * (nunits + 2) * 16;
     };
     while (KS < 8 && xbytes(KS, mb) > (size_t)kSmemBudget && a.nchunk >= 2 * KS) KS *= 2;
-    while (mb > 8 && xbytes(KS, mb) > (size_t)kSmemBudget) mb = (mb + 1) / 2;
-    if (xbytes(KS, mb) > 200 * 1024) return fail(ORCH_ERR_UNSUPPORTED, "K too large for the decode GEMM");
+    // a larger shared-memory slice (fewer CTAs per SM) beats splitting M, which re-reads weights
+    while (mb > 8 && xbytes(KS, mb) > (size_t)kSmemMax) mb = (mb + 1) / 2;
+    if (xbytes(KS, mb) > (size_t)kSmemMax) return fail(ORCH_ERR_UNSUPPORTED, "K too large for the decode GEMM");
     const int nt = (mb + 7) / 8;
     const int ntr = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : 8;
     const size_t redb = (size_t)8 * ntr * (rows_per_cta(mb) + 4) * 4;

@@ -1,6 +1,8 @@
 // Arguments of the quantised skinny-GEMM kernel family (qgemm.cu).
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "orch_common.cuh"
 
 namespace orch {
@@ -35,5 +37,125 @@ struct QArgs {
 
 template <int WF, int EPI>
 int qgemm_run(QArgs a, cudaStream_t st);
+
+// Tensor-core (tcgen05) path for INT4, M >= 16; returns ORCH_ERR_UNSUPPORTED when the
+// shape is outside what it implements.
+template <int EPI>
+int tc_qgemm_run(QArgs a, cudaStream_t st);
+// Activation-row count from which INT4 GEMMs take the tensor-core path (0 = never).
+uint32_t tc_min_m();
+
+namespace cg = cooperative_groups;
+
+// LoRA term of output column `col` of region `reg` (R regions of width `width`):
+// sum_q t[n, reg, q] * B[reg, q, col].
+template <int R>
+__device__ __forceinline__ float lora_delta_r(const QArgs& a, int n, int reg, int col, int width) {
+  const float* t = a.lora_t + ((size_t)n * R + reg) * a.lora_r;
+  const float* bm = a.lora_b + (size_t)reg * a.lora_r * width + col;
+  float v = 0.f;
+  for (int q = 0; q < a.lora_r; ++q) v = fmaf(t[q], bm[(size_t)q * width], v);
+  return v;
+}
+
+// Split-K reduction over the cluster (distributed shared memory) and the fused epilogue.
+// `red` holds this CTA's partial tile as red[n * (ROWS + 4) + row_in_tile] (fp32).
+template <int WF, int EPI, int ROWS>
+__device__ __forceinline__ void qgemm_epilogue(const QArgs& a, float* red, int KS, int ks, int R0) {
+  auto lora_delta = [](const QArgs& aa, int n, int reg, int col, int width) {
+    constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
+    return lora_delta_r<R>(aa, n, reg, col, width);
+  };
+  constexpr int LDR = ROWS + 4;
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+
+  auto total = [&](int n, int rl) {
+    float v = 0.f;
+    for (int r = 0; r < KS; ++r) v += cl.map_shared_rank(red, r)[n * LDR + rl];
+    return v;
+  };
+
+  if (EPI == EPI_STORE || EPI == EPI_RESID) {
+    const int items = a.M * ROWS;
+    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+      const int n = i / ROWS, rl = i - n * ROWS;
+      const int row = R0 + rl;
+      if (row >= a.N) continue;
+      float v = total(n, rl);
+      if (WF == W_Q8PC) v *= __half2float(a.s[row]);
+      if (a.lora_t != nullptr) v += lora_delta(a, n, 0, row, a.N);
+      const size_t o = (size_t)n * a.ldo + row;
+      if (EPI == EPI_RESID) {
+        float* y = static_cast<float*>(a.out);
+        y[o] = y[o] + v;
+      } else if (a.out_f32) {
+        static_cast<float*>(a.out)[o] = v;
+      } else {
+        static_cast<__half*>(a.out)[o] = __float2half_rn(v);
+      }
+    }
+  } else if (EPI == EPI_SWIGLU) {
+    const int F = a.N >> 1;
+    const int items = a.M * (ROWS / 2);
+    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+      const int n = i / (ROWS / 2), jj = i - n * (ROWS / 2);
+      const int b = jj >> 4, ii = jj & 15;
+      const int j = (R0 >> 1) + 16 * b + ii;
+      if (j >= F) continue;
+      float gt = total(n, 32 * b + ii);
+      float up = total(n, 32 * b + 16 + ii);
+      if (a.lora_t != nullptr) {
+        gt += lora_delta(a, n, 0, j, F);
+        up += lora_delta(a, n, 1, j, F);
+      }
+      const float si = gt / (1.0f + expf(-gt));
+      static_cast<__half*>(a.out)[(size_t)n * F + j] = __float2half_rn(si * up);
+    }
+  } else {  // EPI_QKV
+    const int items = a.M * (ROWS / 2);
+    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
+    const int half_hd = a.hd >> 1;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+      const int n = i / (ROWS / 2), pr = i - n * (ROWS / 2);
+      const int row = R0 + 2 * pr;
+      if (row >= a.N) continue;
+      const int region = row / a.H;
+      const int rr = row - region * a.H;
+      const int head = rr / a.hd, d = rr - head * a.hd;
+      float v0 = total(n, 2 * pr), v1 = total(n, 2 * pr + 1);
+      if (a.lora_t != nullptr) {
+        v0 += lora_delta(a, n, region, rr, a.H);
+        v1 += lora_delta(a, n, region, rr + 1, a.H);
+      }
+      const int p = a.pos[n];
+      if (p < 0 || p >= a.max_seq || p >= a.max_pos) {
+        atomicOr(a.check, 1u);
+        continue;
+      }
+      if (region < 2) {
+        const float cs = a.cos_tab[(size_t)p * half_hd + (d >> 1)];
+        const float sn = a.sin_tab[(size_t)p * half_hd + (d >> 1)];
+        const float r0 = v0 * cs - v1 * sn;
+        const float r1 = v0 * sn + v1 * cs;
+        v0 = r0;
+        v1 = r1;
+      }
+      const __half2 hv = __floats2half2_rn(v0, v1);
+      if (region == 0) {
+        *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
+      } else {
+        const int slot = a.slots ? a.slots[n] : n;
+        __half* cache = region == 1 ? a.kc : a.vc;
+        const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
+        *reinterpret_cast<__half2*>(cache + off) = hv;
+      }
+    }
+  }
+  cl.sync();
+}
+
 
 }  // namespace orch

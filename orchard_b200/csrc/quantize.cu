@@ -44,6 +44,8 @@ __device__ __forceinline__ void load32<__half>(const __half* p, float (&v)[32]) 
 
 template <typename T>
 __global__ void quant_q4_kernel(const T* w, uint8_t* packed, __half* scales, size_t groups) {
+  pdl_trigger();
+  pdl_wait();
   for (size_t gi = blockIdx.x * (size_t)blockDim.x + threadIdx.x; gi < groups;
        gi += (size_t)gridDim.x * blockDim.x) {
     float v[32];
@@ -70,6 +72,8 @@ __global__ void quant_q4_kernel(const T* w, uint8_t* packed, __half* scales, siz
 // One group of `gs` consecutive weights per warp (gs = 32 or the row length).
 template <typename T>
 __global__ void quant_q8_kernel(const T* w, int8_t* q, __half* scales, size_t groups, int gs) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -110,11 +114,11 @@ extern "C" int orch_quantize_q4_0(const void* w, int w_dt, void* packed, void* s
   const size_t groups = (size_t)N * (K / 32);
   cudaStream_t st = as_stream(stream);
   if (w_dt == ORCH_F32)
-    quant_q4_kernel<float><<<qgrid(groups, 128), 128, 0, st>>>((const float*)w, (uint8_t*)packed,
-                                                               (__half*)scales, groups);
+    ORCH_CUDA(launch_k(quant_q4_kernel<float>, dim3(qgrid(groups, 128)), dim3(128), 0, st, dim3(0, 0, 0), (const float*)w, (uint8_t*)packed,
+                                                               (__half*)scales, groups));
   else if (w_dt == ORCH_F16)
-    quant_q4_kernel<__half><<<qgrid(groups, 128), 128, 0, st>>>((const __half*)w, (uint8_t*)packed,
-                                                                (__half*)scales, groups);
+    ORCH_CUDA(launch_k(quant_q4_kernel<__half>, dim3(qgrid(groups, 128)), dim3(128), 0, st, dim3(0, 0, 0), (const __half*)w, (uint8_t*)packed,
+                                                                (__half*)scales, groups));
   else
     return fail(ORCH_ERR_INVALID, "quantize_q4_0: bad dtype");
   return check_launch("quantize_q4_0");
@@ -124,9 +128,9 @@ static int quant_q8(const void* w, int w_dt, void* q, void* scales, size_t group
   cudaStream_t st = as_stream(stream);
   const int g = qgrid(groups * 32, 256);
   if (w_dt == ORCH_F32)
-    quant_q8_kernel<float><<<g, 256, 0, st>>>((const float*)w, (int8_t*)q, (__half*)scales, groups, gs);
+    ORCH_CUDA(launch_k(quant_q8_kernel<float>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const float*)w, (int8_t*)q, (__half*)scales, groups, gs));
   else if (w_dt == ORCH_F16)
-    quant_q8_kernel<__half><<<g, 256, 0, st>>>((const __half*)w, (int8_t*)q, (__half*)scales, groups, gs);
+    ORCH_CUDA(launch_k(quant_q8_kernel<__half>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), (const __half*)w, (int8_t*)q, (__half*)scales, groups, gs));
   else
     return fail(ORCH_ERR_INVALID, "quantize_q8: bad dtype");
   return check_launch("quantize_q8");

@@ -1,0 +1,124 @@
+"""Kernel-level timing of the decode path's kernels at the 7B shapes.
+
+    python -m orchard_b200.kbench [--kernel q4|q8pc|attn|all] [--M 1,16,64] [--reps 50]
+
+Each INT4/INT8 GEMM shape is timed over enough distinct weight copies that the set
+exceeds the 126 MB L2 (so every launch streams its weights from HBM), with CUDA events on
+the launching stream after warm-up. Reported GB/s use the algorithmic bytes: packed
+weights + scales + activations in + outputs out. One JSON line per case.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib
+from ._lib import F16, F32, call
+
+DECODE_SHAPES = [("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 22016), ("down", 11008, 4096),
+                 ("lm_head", 4096, 32000)]
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _graph_time(run, n: int, reps: int) -> float:
+    """Microseconds per launch: `reps` launches (rotating over `n` inputs) captured in one
+    CUDA graph and replayed, so host launch overhead is not measured."""
+    for i in range(2 * n):
+        run(i)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for i in range(reps):
+            run(i)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1000 / reps
+
+
+def _copies(nbytes: int) -> int:
+    return max(2, -(-4 * L2_BYTES // nbytes))
+
+
+def time_q4(M: int, K: int, N: int, reps: int, fmt: str = "q4"):
+    dev = "cuda"
+    wbytes = N * K // 2 if fmt == "q4" else N * K
+    sbytes = N * K // 16 if fmt == "q4" else 2 * N
+    n = min(_copies(wbytes + sbytes), 64)
+    ws = []
+    for i in range(n):
+        if fmt == "q4":
+            w = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev)
+            s = (torch.rand((N, K // 32), device=dev) * 0.01).half()
+        else:
+            w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
+            s = (torch.rand(N, device=dev) * 0.01).half()
+        ws.append((w, s))
+    x = torch.randn((M, K), device=dev).half()
+    y = torch.empty((M, N), device=dev, dtype=torch.float32)
+    fn = "orch_gemm_q4_0_ex" if fmt == "q4" else "orch_gemm_q8_pc"
+
+    def run(i):
+        w, s = ws[i % n]
+        call(fn, w, s, x, F16, y, F32, K, N, M, torch.cuda.current_stream().cuda_stream)
+
+    us = _graph_time(run, n, reps)
+    byts = wbytes + sbytes + 2 * M * K + 4 * M * N
+    return {"kernel": f"qgemm_{fmt}", "M": M, "K": K, "N": N, "us": round(us, 3),
+            "GBps": round(byts / us / 1e3, 1), "bytes": byts, "weight_copies": n}
+
+
+def time_attn(M: int, L: int, reps: int, nh: int = 32, hd: int = 128, max_seq: int = 640):
+    dev = "cuda"
+    n = max(1, min(16, -(-4 * L2_BYTES // (2 * M * nh * max_seq * hd * 2))))
+    caches = [(torch.randn((M, nh, max_seq, hd), device=dev).half(), torch.randn((M, nh, max_seq, hd), device=dev).half())
+              for _ in range(n)]
+    q = torch.randn((M, nh * hd), device=dev).half()
+    out = torch.empty_like(q)
+    pos = torch.full((M,), L - 1, dtype=torch.int32, device=dev)
+    wsb = _lib.lib().orch_attention_workspace_bytes(M, nh, hd, max_seq)
+    ws = torch.empty(max(wsb // 4, 1), dtype=torch.float32, device=dev)
+    def run(i):
+        kc, vc = caches[i % n]
+        call("orch_attention_decode", q, kc, vc, pos, None, out, M, nh, hd, max_seq, ws, wsb,
+             torch.cuda.current_stream().cuda_stream)
+
+    us = _graph_time(run, n, reps)
+    byts = 2 * M * nh * L * hd * 2 + 2 * 2 * M * nh * hd
+    return {"kernel": "attention_decode", "M": M, "L": L, "us": round(us, 3), "GBps": round(byts / us / 1e3, 1),
+            "bytes": byts, "cache_copies": n}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default="all", choices=["q4", "q8pc", "attn", "all"])
+    ap.add_argument("--M", default="1,16,64")
+    ap.add_argument("--shape", default="", help="only this decode shape name (qkv, o, gate_up, down, lm_head)")
+    ap.add_argument("--reps", type=int, default=50)
+    a = ap.parse_args()
+    call("orch_init", 0, None)
+    Ms = [int(v) for v in a.M.split(",")]
+    for M in Ms:
+        if a.kernel in ("q4", "q8pc", "all"):
+            for name, K, N in DECODE_SHAPES:
+                if a.shape and name != a.shape:
+                    continue
+                for fmt in (("q4", "q8pc") if a.kernel == "all" else (a.kernel,)):
+                    r = time_q4(M, K, N, a.reps, fmt)
+                    r["shape"] = name
+                    print(json.dumps(r), flush=True)
+        if a.kernel in ("attn", "all"):
+            print(json.dumps(time_attn(M, 577, a.reps)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
