@@ -234,27 +234,26 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
     compute(ch + U, wb, sb);
   }
 
-  // ---- partial tile -> shared memory: red[n][row] (fp32) --------------------------------
-  __syncthreads();
-  float* red = reinterpret_cast<float*>(sm);
-  constexpr int LDR = ROWS + 4;
+  // ---- partials -> owners' receive buffers (they alias the staged activations) ----------
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  float* recv = reinterpret_cast<float*>(sm);
+  const int Mp = epi_mp(a.M);
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
     const int rl = warp * 16 * MT + mt * 16 + g;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int n0 = nt * 8 + 2 * c;
-      if (n0 < a.M) {
-        red[n0 * LDR + rl] = acc[mt][nt][0];
-        red[n0 * LDR + rl + 8] = acc[mt][nt][2];
-      }
-      if (n0 + 1 < a.M) {
-        red[(n0 + 1) * LDR + rl] = acc[mt][nt][1];
-        red[(n0 + 1) * LDR + rl + 8] = acc[mt][nt][3];
+      if (n0 < Mp) {  // Mp is a multiple of 4, so n0 + 1 < Mp too
+        *reinterpret_cast<float2*>(epi_dest<EPI, ROWS>(cl, recv, Mp, KS, ks, rl, n0)) =
+            make_float2(acc[mt][nt][0], acc[mt][nt][1]);
+        *reinterpret_cast<float2*>(epi_dest<EPI, ROWS>(cl, recv, Mp, KS, ks, rl + 8, n0)) =
+            make_float2(acc[mt][nt][2], acc[mt][nt][3]);
       }
     }
   }
-  qgemm_epilogue<WF, EPI, ROWS>(a, red, KS, ks, R0);
+  qgemm_finish<WF, EPI, ROWS>(a, recv, KS, ks, R0);
 }
 
 // ------------------------------------------------------------------------------------
@@ -323,9 +322,7 @@ int qgemm_run(QArgs a, cudaStream_t st) {
     // a larger shared-memory slice (fewer CTAs per SM) beats splitting M, which re-reads weights
     while (mb > 8 && xbytes(KS, mb) > (size_t)kSmemMax) mb = (mb + 1) / 2;
     if (xbytes(KS, mb) > (size_t)kSmemMax) return fail(ORCH_ERR_UNSUPPORTED, "K too large for the decode GEMM");
-    const int nt = (mb + 7) / 8;
-    const int ntr = nt <= 1 ? 1 : nt <= 2 ? 2 : nt <= 4 ? 4 : 8;
-    const size_t redb = (size_t)8 * ntr * (rows_per_cta(mb) + 4) * 4;
+    const size_t redb = (size_t)4 * (rows_per_cta(mb) == 128 ? epi_recv_floats<128>(mb) : epi_recv_floats<64>(mb));
     const size_t smem = std::max(xbytes(KS, mb), redb);
     b.M = mb;
     // advance per-row pointers

@@ -58,32 +58,78 @@ __device__ __forceinline__ float lora_delta_r(const QArgs& a, int n, int reg, in
   return v;
 }
 
-// Split-K reduction over the cluster (distributed shared memory) and the fused epilogue.
-// `red` holds this CTA's partial tile as red[n * (ROWS + 4) + row_in_tile] (fp32).
+// ---- split-K reduce-scatter over the cluster and the fused epilogue ----------------------
+// An epilogue item row is one weight row (STORE/RESID), a rotation pair of rows 2p, 2p+1
+// (QKV) or the gate and up rows of one output (SWIGLU, rows 32b+i and 32b+16+i). The ROWS/E
+// item rows of a tile are owned in equal contiguous blocks of IRL = ROWS/E/KS by the KS
+// CTAs of the cluster. Each CTA pushes its partial sums into the owners' receive buffers
+// with distributed-shared-memory vector stores (no remote loads); after one cluster barrier
+// every owner sums its KS slices locally and runs the epilogue, consecutive threads on
+// consecutive rows. Receive buffer of an owner: [src][irl][e][Mp] floats, Mp = M rounded
+// up to 4 (ROWS * Mp floats in total).
+template <int EPI>
+__host__ __device__ constexpr int epi_elems() { return (EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 1; }
+
+__host__ __device__ __forceinline__ int epi_mp(int M) { return (M + 3) & ~3; }
+
+template <int ROWS>
+__host__ __device__ __forceinline__ int epi_recv_floats(int M) { return ROWS * epi_mp(M); }
+
+template <int EPI>
+__device__ __forceinline__ int epi_item_row(int rl, int& e) {
+  if (EPI == EPI_QKV) {
+    e = rl & 1;
+    return rl >> 1;
+  }
+  if (EPI == EPI_SWIGLU) {
+    const int w = rl & 31;
+    e = w >> 4;
+    return (rl >> 5) * 16 + (w & 15);
+  }
+  e = 0;
+  return rl;
+}
+
+// Destination of the partial sums of tile row `rl` for activation rows n..n+W-1 (n % W == 0).
+template <int EPI, int ROWS>
+__device__ __forceinline__ float* epi_dest(cg::cluster_group& cl, float* recv, int Mp, int KS, int ks, int rl,
+                                           int n) {
+  constexpr int E = epi_elems<EPI>();
+  constexpr int IR = ROWS / E;
+  const int IRL = IR / KS;  // KS is a power of two <= IR
+  int e;
+  const int irow = epi_item_row<EPI>(rl, e);
+  const int q = irow / IRL, irl = irow - q * IRL;
+  float* base = (q == ks) ? recv : cl.map_shared_rank(recv, q);
+  return base + ((ks * IRL + irl) * E + e) * Mp + n;
+}
+
+// After every CTA of the cluster pushed its partials: the cluster barrier, then the sums and
+// the epilogue of this CTA's item rows.
 template <int WF, int EPI, int ROWS>
-__device__ __forceinline__ void qgemm_epilogue(const QArgs& a, float* red, int KS, int ks, int R0) {
+__device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, int KS, int ks, int R0) {
   auto lora_delta = [](const QArgs& aa, int n, int reg, int col, int width) {
     constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
     return lora_delta_r<R>(aa, n, reg, col, width);
   };
-  constexpr int LDR = ROWS + 4;
-  cg::cluster_group cl = cg::this_cluster();
-  cl.sync();
-
-  auto total = [&](int n, int rl) {
+  constexpr int E = epi_elems<EPI>();
+  constexpr int IR = ROWS / E;
+  cg::this_cluster().sync();
+  const int IRL = IR / KS;
+  const int IRL_LOG = __ffs(IRL) - 1;
+  const int Mp = epi_mp(a.M);
+  const int items = IRL * a.M;
+  auto total = [&](int irl, int n, int e) {
     float v = 0.f;
-    for (int r = 0; r < KS; ++r) v += cl.map_shared_rank(red, r)[n * LDR + rl];
+    for (int r = 0; r < KS; ++r) v += recv[((r * IRL + irl) * E + e) * Mp + n];
     return v;
   };
-
   if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    const int items = a.M * ROWS;
-    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
-    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-      const int n = i / ROWS, rl = i - n * ROWS;
-      const int row = R0 + rl;
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+      const int row = R0 + ks * IRL + irl;
       if (row >= a.N) continue;
-      float v = total(n, rl);
+      float v = total(irl, n, 0);
       if (WF == W_Q8PC) v *= __half2float(a.s[row]);
       if (a.lora_t != nullptr) v += lora_delta(a, n, 0, row, a.N);
       const size_t o = (size_t)n * a.ldo + row;
@@ -98,15 +144,12 @@ __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, float* red, int K
     }
   } else if (EPI == EPI_SWIGLU) {
     const int F = a.N >> 1;
-    const int items = a.M * (ROWS / 2);
-    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
-    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-      const int n = i / (ROWS / 2), jj = i - n * (ROWS / 2);
-      const int b = jj >> 4, ii = jj & 15;
-      const int j = (R0 >> 1) + 16 * b + ii;
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+      const int j = (R0 >> 1) + ks * IRL + irl;
       if (j >= F) continue;
-      float gt = total(n, 32 * b + ii);
-      float up = total(n, 32 * b + 16 + ii);
+      float gt = total(irl, n, 0);
+      float up = total(irl, n, 1);
       if (a.lora_t != nullptr) {
         gt += lora_delta(a, n, 0, j, F);
         up += lora_delta(a, n, 1, j, F);
@@ -115,17 +158,15 @@ __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, float* red, int K
       static_cast<__half*>(a.out)[(size_t)n * F + j] = __float2half_rn(si * up);
     }
   } else {  // EPI_QKV
-    const int items = a.M * (ROWS / 2);
-    const int i0 = (ks * items) / KS, i1 = ((ks + 1) * items) / KS;
     const int half_hd = a.hd >> 1;
-    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-      const int n = i / (ROWS / 2), pr = i - n * (ROWS / 2);
-      const int row = R0 + 2 * pr;
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+      const int row = R0 + 2 * (ks * IRL + irl);
       if (row >= a.N) continue;
       const int region = row / a.H;
       const int rr = row - region * a.H;
       const int head = rr / a.hd, d = rr - head * a.hd;
-      float v0 = total(n, 2 * pr), v1 = total(n, 2 * pr + 1);
+      float v0 = total(irl, n, 0), v1 = total(irl, n, 1);
       if (a.lora_t != nullptr) {
         v0 += lora_delta(a, n, region, rr, a.H);
         v1 += lora_delta(a, n, region, rr + 1, a.H);
@@ -154,8 +195,6 @@ __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, float* red, int K
       }
     }
   }
-  cl.sync();
 }
-
 
 }  // namespace orch

@@ -140,148 +140,211 @@ __device__ __forceinline__ uint4 dq8_natural(uint32_t w, uint32_t sc) {
   return o;
 }
 
+// Bounded wait that also gives up as soon as another role of the CTA has failed.
+__device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, volatile int* failed) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  while (!mbar_try(bar, parity)) {
+    if (*failed || gtimer() - t0 > kWaitNs) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+constexpr int kWBytes = kTcRows * (kTcBK / 2);  // packed INT4 tile: 128 rows x 32 bytes
+constexpr int kSBytes = kTcRows * 16;           // scales for 4 stages: 128 rows x 8 fp16
+constexpr int kARing = 2;
+constexpr int kSRing = 4;
+constexpr int kWarpsDq = 8;                       // dequantisation warps (0-3 also run the epilogue)
+constexpr int kWarpProd = kWarpsDq;               // TMA producer warp
+constexpr int kWarpMma = kWarpsDq + 1;            // MMA issuer warp
+constexpr int kTcThreads2 = (kWarpsDq + 2) * 32;
+
+template <int NTILE>
+struct TcCfg {
+  static constexpr int S = NTILE <= 32 ? 8 : (NTILE <= 64 ? 6 : 4);  // TMA ring stages
+  static constexpr int AHEAD = S - 2;                                 // stages in flight
+  static constexpr int XBytes = NTILE * kTcBK * 2;
+  static constexpr int OffA = 0;
+  static constexpr int OffX = OffA + kARing * kTcABytes;
+  static constexpr int OffW = OffX + S * XBytes;
+  static constexpr int OffS = OffW + S * kWBytes;
+  static constexpr int OffBar = OffS + kSRing * kSBytes;
+  static constexpr int Bytes = OffBar + 256;
+};
+
 template <int EPI, int NTILE>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmx,
-                                                                 const QArgs a0) {
+__global__ void __launch_bounds__(kTcThreads2, 1)
+    tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                    const __grid_constant__ CUtensorMap tms, const QArgs a0) {
+  using C = TcCfg<NTILE>;
   extern __shared__ __align__(1024) uint8_t smraw[];
-  constexpr int kBBytes = NTILE * kTcBK * 2;
   constexpr uint32_t kCols = NTILE < 32 ? 32 : NTILE;
   constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NTILE >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = sm;
-  uint8_t* sB = sm + kTcStages * kTcABytes;
-  uint64_t* full_b = reinterpret_cast<uint64_t*>(sB + kTcStages * kBBytes);
-  uint64_t* empty = full_b + kTcStages;
-  uint64_t* done = empty + kTcStages;
+  uint8_t* sA = sm + C::OffA;
+  uint8_t* sX = sm + C::OffX;
+  uint8_t* sW = sm + C::OffW;
+  uint8_t* sS = sm + C::OffS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OffBar);
+  uint64_t* empty = full + C::S;
+  uint64_t* afull = empty + C::S;
+  uint64_t* aempty = afull + kARing;
+  uint64_t* done = aempty + kARing;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KS = gridDim.y, ks = blockIdx.y;
   const int R0 = blockIdx.x * kTcRows;
   const int tok0 = blockIdx.z * NTILE;
+  // K is split over the cluster in blocks of 4 stages (one scale tile per block)
   const int nst_total = (a0.K + kTcBK - 1) / kTcBK;
-  const int st0 = (ks * nst_total) / KS, st1 = ((ks + 1) * nst_total) / KS;
+  const int nblk = (nst_total + 3) / 4;
+  const int st0 = ((ks * nblk) / KS) * 4;
+  const int st1 = min(nst_total, (((ks + 1) * nblk) / KS) * 4);
   const int nst = st1 - st0;
-  const int row = R0 + tid;
-  const bool row_ok = row < a0.N;
-  const int G = a0.K >> 5;
-  const uint8_t* wrow = a0.w + (size_t)(row_ok ? row : 0) * (size_t)(a0.K >> 1);
-  const __half* srow = a0.s + (size_t)(row_ok ? row : 0) * G;
-
-  // this row's packed weights for one stage: 2 x 16 bytes (64 k) + two group scales
-  auto wload = [&](int s, uint4& w0, uint4& w1, uint32_t& s0, uint32_t& s1) {
-    const int k0 = (st0 + s) * kTcBK;
-    const uint4 fill = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-    w0 = fill;
-    w1 = fill;
-    s0 = 0;
-    s1 = 0;
-    if (s < nst && row_ok) {
-      const uint8_t* p = wrow + (k0 >> 1);
-      w0 = ld_stream16(p);
-      s0 = h2_bits(__half2half2(srow[k0 >> 5]));
-      if (k0 + 32 < a0.K) {
-        w1 = ld_stream16(p + 16);
-        s1 = h2_bits(__half2half2(srow[(k0 >> 5) + 1]));
-      }
-    }
-  };
-
-  uint4 wA[kTcStages], wB[kTcStages];
-  uint32_t sc0[kTcStages], sc1[kTcStages];
 
   if (warp == 0) tmem_alloc(tmem_slot, kCols);
   if (tid == 0) {
-    for (int i = 0; i < kTcStages; ++i) {
-      mbar_init(&full_b[i], 1);
+    for (int i = 0; i < C::S; ++i) {
+      mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < kARing; ++i) {
+      mbar_init(&afull[i], kWarpsDq * 32);  // every dequantisation thread arrives
+      mbar_init(&aempty[i], 1);
     }
     mbar_init(done, 1);
     *failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     fence_proxy_async();
   }
-  // Weights do not depend on the previous kernel: request the first stages before waiting.
-#pragma unroll
-  for (int u = 0; u < kTcStages; ++u) wload(u, wA[u], wB[u], sc0[u], sc1[u]);
   pdl_trigger();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
-  pdl_wait();
 
-  int pend_slot = -1;  // thread 0: slot whose TMA load was issued but not yet waited for
-  uint32_t pend_par = 0;
-  for (int s0 = 0; s0 < nst; s0 += kTcStages) {
-#pragma unroll
-    for (int u = 0; u < kTcStages; ++u) {
-      const int s = s0 + u;
-      if (s >= nst) break;
-      const uint32_t it = (uint32_t)(s / kTcStages);
-      if (s >= kTcStages && !mbar_wait(&empty[u], (it - 1) & 1)) *failed = 1;
-      if (tid == 0 && !*failed) {
-        mbar_expect_tx(&full_b[u], kBBytes);
-        tma_load_2d(sB + u * kBBytes, &tmx, &full_b[u], (st0 + s) * kTcBK, tok0);
-        pend_slot = u;
-        pend_par = it & 1;
-      }
-      // dequantise this row's 64 weights into the swizzled A tile
-      {
-        uint8_t* arow = sA + u * kTcABytes + (tid >> 3) * 1024 + (tid & 7) * 128;
-        const uint32_t wv[8] = {wA[u].x, wA[u].y, wA[u].z, wA[u].w, wB[u].x, wB[u].y, wB[u].z, wB[u].w};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = dq8_natural(wv[c], c < 4 ? sc0[u] : sc1[u]);
-          *reinterpret_cast<uint4*>(arow + ((c ^ (tid & 7)) << 4)) = v;
-        }
-      }
-      wload(s + kTcStages, wA[u], wB[u], sc0[u], sc1[u]);
-      fence_proxy_async();
-      __syncthreads();
-      if (*failed) break;
-      if (tid == 0) {
-        if (!mbar_wait(&full_b[u], it & 1)) {
+  bool done_ok = true;
+  if (warp == kWarpProd) {
+    // ---------------- TMA producer: one thread, runs up to S - 2 stages ahead ----------------
+    if (lane == 0) {
+      int issued = 0;
+      auto load_wx = [&](int p, bool with_x) {
+        const int v = p % C::S;
+        const bool with_s = (p & 3) == 0;
+        const int k0 = (st0 + p) * kTcBK;
+        mbar_expect_tx(&full[v], (uint32_t)(kWBytes + C::XBytes + (with_s ? kSBytes : 0)));
+        tma_load_2d(sW + v * kWBytes, &tmw, &full[v], k0 >> 1, R0);
+        if (with_s) tma_load_2d(sS + ((p >> 2) % kSRing) * kSBytes, &tms, &full[v], k0 >> 5, R0);
+        if (with_x) tma_load_2d(sX + v * C::XBytes, &tmx, &full[v], k0, tok0);
+      };
+      // weights and scales do not depend on the previous kernel: start streaming them first
+      const int pre = min(C::AHEAD, nst);
+      for (int p = 0; p < pre; ++p) load_wx(p, false);
+      pdl_wait();  // activations may come from the previous kernel
+      for (int p = 0; p < pre; ++p) tma_load_2d(sX + p * C::XBytes, &tmx, &full[p], (st0 + p) * kTcBK, tok0);
+      issued = pre;
+      for (int p = pre; p < nst && !*failed; ++p) {
+        const int v = p % C::S;
+        if (p >= C::S && !mbar_wait_f(&empty[v], (uint32_t)(p / C::S - 1) & 1, failed)) {
           *failed = 1;
-        } else {
-          pend_slot = -1;
-          tc_fence_after();
-          const uint64_t ad = sw128_desc(smem_u32(sA + u * kTcABytes));
-          const uint64_t bd = sw128_desc(smem_u32(sB + u * kBBytes));
-#pragma unroll
-          for (int kk = 0; kk < kTcBK / 16; ++kk)
-            umma_f16(tmem_d, ad + 2 * kk, bd + 2 * kk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[u]);
+          break;
         }
+        load_wx(p, true);
+        issued = p + 1;
       }
+      // loads still in flight when the consumers gave up: wait for them before exiting
+      if (*failed)
+        for (int p = max(0, issued - C::S); p < issued; ++p) mbar_wait(&full[p % C::S], (uint32_t)(p / C::S) & 1);
+    } else {
+      pdl_wait();
     }
-    __syncthreads();
-    if (*failed) break;
+  } else if (warp == kWarpMma) {
+    // ---------------- MMA issuer: one thread ----------------
+    pdl_wait();
+    if (lane == 0) {
+      for (int s = 0; s < nst && !*failed; ++s) {
+        const int v = s % C::S, ai = s % kARing;
+        if (!mbar_wait_f(&full[v], (uint32_t)(s / C::S) & 1, failed) ||
+            !mbar_wait_f(&afull[ai], (uint32_t)(s / kARing) & 1, failed)) {
+          *failed = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(smem_u32(sA + ai * kTcABytes));
+        const uint64_t bd = sw128_desc(smem_u32(sX + v * C::XBytes));
+#pragma unroll
+        for (int kk = 0; kk < kTcBK / 16; ++kk)
+          umma_f16(tmem_d, ad + 2 * kk, bd + 2 * kk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[v]);
+        umma_commit(&aempty[ai]);
+      }
+      umma_commit(done);
+    }
+  } else {
+    // ---------------- dequantisation warps: packed tile -> swizzled fp16 A tile ----------------
+    pdl_wait();
+    const int rs = lane >> 3, c = lane & 7;
+    for (int s = 0; s < nst; ++s) {
+      const int v = s % C::S, ai = s % kARing;
+      if (!mbar_wait_f(&full[v], (uint32_t)(s / C::S) & 1, failed)) {
+        *failed = 1;
+        break;
+      }
+      if (s >= kARing && !mbar_wait_f(&aempty[ai], (uint32_t)(s / kARing - 1) & 1, failed)) {
+        *failed = 1;
+        break;
+      }
+      const uint8_t* wt = sW + v * kWBytes;
+      const __half* st = reinterpret_cast<const __half*>(sS + ((s >> 2) % kSRing) * kSBytes);
+      uint8_t* at = sA + ai * kTcABytes;
+      const int sj = (s & 3) * 2 + (c >> 2);
+#pragma unroll
+      for (int i = 0; i < kTcRows / (4 * kWarpsDq); ++i) {
+        const int r = warp * (kTcRows / kWarpsDq) + 4 * i + rs;
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(wt + r * 32 + c * 4);
+        const uint32_t sc = h2_bits(__half2half2(st[r * 8 + sj]));
+        *reinterpret_cast<uint4*>(at + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
+            dq8_natural(w, sc);
+      }
+      fence_proxy_async();
+      mbar_arrive(&afull[ai]);
+    }
   }
-  // all MMAs issued by thread 0 -> done barrier; every thread waits (bounded)
-  if (tid == 0) umma_commit(done);
-  const bool done_ok = mbar_wait(done, 0);
-  if (tid == 0 && pend_slot >= 0) mbar_wait(&full_b[pend_slot], pend_par);  // drain after a failure
+  done_ok = mbar_wait(done, 0);
   tc_fence_after();
 
-  // accumulator -> shared-memory partial tile red[n][row] (the ring is no longer in use)
-  float* red = reinterpret_cast<float*>(sm);
-  constexpr int LDR = kTcRows + 4;
+  // accumulator rows -> owners' receive buffers (they alias the rings: wait for the cluster)
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  float* recv = reinterpret_cast<float*>(sm);
   const int mcount = min(NTILE, a0.M - tok0);
+  const bool bad = *failed || !done_ok;
+  const int Mp = epi_mp(mcount);
+  if (warp < 4) {  // TMEM lanes 32w..32w+31 belong to warp w (w = 0..3)
 #pragma unroll 1
-  for (int c = 0; c < NTILE; c += 16) {
-    uint32_t r[16];
-    tmem_ld16(tmem_d + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, r);
+    for (int cc = 0; cc < Mp; cc += 16) {
+      uint32_t r[16];
+      tmem_ld16(tmem_d + ((uint32_t)(32 * warp) << 16) + (uint32_t)cc, r);
+      float* dst = epi_dest<EPI, kTcRows>(cl, recv, Mp, KS, ks, tid, cc);
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (c + j < mcount) red[(c + j) * LDR + tid] = (*failed || !done_ok) ? 0.f : __uint_as_float(r[j]);
+      for (int j = 0; j < 16; j += 4)
+        if (cc + j < Mp)
+          *reinterpret_cast<float4*>(dst + j) =
+              bad ? make_float4(0.f, 0.f, 0.f, 0.f)
+                  : make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                __uint_as_float(r[j + 3]));
+    }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, kCols);
-  if (tid == 0 && (*failed || !done_ok)) atomicOr(a0.check, 256u);
+  if (tid == 0 && bad) atomicOr(a0.check, 256u);
 
   QArgs a = a0;
   a.M = mcount;
@@ -297,7 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_qgemm_kernel(const __grid_co
     a.pos = a0.pos + tok0;
     if (a0.slots) a.slots = a0.slots + tok0;
   }
-  qgemm_epilogue<W_Q4, EPI, kTcRows>(a, red, KS, ks, R0);
+  qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -321,20 +384,39 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-size_t tc_smem(int ntile) { return (size_t)kTcStages * (kTcABytes + ntile * kTcBK * 2) + 1024 + 256; }
+bool encode2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  const cuuint64_t gdim[2] = {inner, outer};
+  const cuuint64_t gstride[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(map, dt, 2, const_cast<void*>(base), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t tc_smem_bytes(int ntile) {
+  switch (ntile) {
+    case 16: return TcCfg<16>::Bytes + 1024;
+    case 32: return TcCfg<32>::Bytes + 1024;
+    case 64: return TcCfg<64>::Bytes + 1024;
+    case 128: return TcCfg<128>::Bytes + 1024;
+    default: return TcCfg<256>::Bytes + 1024;
+  }
+}
 
 template <int EPI, int NTILE>
-int tc_launch(const CUtensorMap& map, const QArgs& a, int KS, cudaStream_t st) {
+int tc_launch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int KS,
+              cudaStream_t st) {
   static bool attr_done[64] = {};
   const int dev = device_index();
   auto kern = tc_qgemm_kernel<EPI, NTILE>;
-  const size_t smem = tc_smem(NTILE);
+  const size_t smem = tc_smem_bytes(NTILE);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     ORCH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_done[dev] = true;
   }
   const dim3 grid((a.N + kTcRows - 1) / kTcRows, KS, (a.M + NTILE - 1) / NTILE);
-  ORCH_CUDA(launch_k(kern, grid, dim3(kTcThreads), smem, st, dim3(1, KS, 1), map, a));
+  ORCH_CUDA(launch_k(kern, grid, dim3(kTcThreads2), smem, st, dim3(1, KS, 1), mx, mw, ms, a));
   return ORCH_OK;
 }
 
@@ -350,32 +432,34 @@ void set_tc_min_m(uint32_t m) { g_tc_min_m = m; }
 
 template <int EPI>
 int tc_qgemm_run(QArgs a, cudaStream_t st) {
-  if (a.x_f32 || a.M < 16 || (a.K % 32) != 0) return ORCH_ERR_UNSUPPORTED;
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return ORCH_ERR_UNSUPPORTED;
-  if (((uintptr_t)a.x & 15) != 0) return ORCH_ERR_UNSUPPORTED;
+  // tensor maps need 16-byte row strides: K % 256 == 0 for the scale rows
+  if (a.x_f32 || a.M < 1 || (a.K % 256) != 0 || !encode_fn()) return ORCH_ERR_UNSUPPORTED;
+  if (((uintptr_t)a.x & 15) != 0 || ((uintptr_t)a.w & 15) != 0 || ((uintptr_t)a.s & 15) != 0)
+    return ORCH_ERR_UNSUPPORTED;
   a.check = device_check_word();
-  const int ntile = a.M <= 32 ? 32 : a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
-  CUtensorMap map;
-  const cuuint64_t gdim[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-  const cuuint64_t gstride[1] = {(cuuint64_t)a.K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)ntile};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), gdim, gstride, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return fail(ORCH_ERR_UNSUPPORTED, "tensor map encode failed");
-  const int nst = (a.K + kTcBK - 1) / kTcBK;
+  const int ntile = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
+  CUtensorMap mx, mw, ms;
+  const bool ok = encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
+                           (uint64_t)a.K * 2, kTcBK, ntile, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
+                           (uint64_t)(a.K / 2), kTcBK / 2, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                  encode2d(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.s, (uint64_t)(a.K / 32), (uint64_t)a.N,
+                           (uint64_t)(a.K / 32) * 2, 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return fail(ORCH_ERR_UNSUPPORTED, "tensor map encode failed");
+  const int nblk = (a.K / kTcBK + 3) / 4;
   const int tiles = ((a.N + kTcRows - 1) / kTcRows) * ((a.M + ntile - 1) / ntile);
-  const int per_sm = tc_smem(ntile) * 2 <= 227 * 1024 ? 2 : 1;
+  const int per_sm = tc_smem_bytes(ntile) * 2 <= 227 * 1024 ? 2 : 1;
+  // split K only as far as one wave of CTAs covers the SMs
+  const int slots = per_sm * num_sms();
   int KS = 1;
-  while (KS < 8 && tiles * KS < per_sm * num_sms() && nst >= 2 * kTcStages * KS) KS *= 2;
+  while (KS < 8 && tiles * KS * 2 <= slots && nblk >= KS * 4) KS *= 2;
   int rc;
   switch (ntile) {
-    case 32: rc = tc_launch<EPI, 32>(map, a, KS, st); break;
-    case 64: rc = tc_launch<EPI, 64>(map, a, KS, st); break;
-    case 128: rc = tc_launch<EPI, 128>(map, a, KS, st); break;
-    default: rc = tc_launch<EPI, 256>(map, a, KS, st); break;
+    case 16: rc = tc_launch<EPI, 16>(mx, mw, ms, a, KS, st); break;
+    case 32: rc = tc_launch<EPI, 32>(mx, mw, ms, a, KS, st); break;
+    case 64: rc = tc_launch<EPI, 64>(mx, mw, ms, a, KS, st); break;
+    case 128: rc = tc_launch<EPI, 128>(mx, mw, ms, a, KS, st); break;
+    default: rc = tc_launch<EPI, 256>(mx, mw, ms, a, KS, st); break;
   }
   if (rc != ORCH_OK) return rc;
   return check_launch("tc_qgemm");
