@@ -178,6 +178,22 @@ int orch_attention_decode(const void* q, const void* k_cache, const void* v_cach
  * kernel (TMEM accumulators, TMA-fed activations); fewer rows use the mma.sync decode
  * kernel. 0 disables the tensor-core kernel. Default 17 (ORCHARD_TC_MIN_M overrides). */
 int orch_set_tc_min_m(uint32_t m);
+/* Decode attention that allocates nothing (no counterpart in the reference). Same inputs,
+ * outputs and arithmetic as orch_attention_decode, but the split-position partials live in
+ * a 1 MiB array inside the library (orch_attention_noalloc_max_bytes()) that every GPU
+ * loading the library keeps until the process exits. For callers that cannot allocate
+ * device memory: hosts capturing CUDA graphs of their own, memory-static real-time hosts,
+ * plugin hosts that pass only the call's tensors. The first call on a device looks up the
+ * array's device address; make it before any stream capture on that device. A shape whose
+ * partials exceed the array fails with ORCH_ERR_UNSUPPORTED. Every call on a device uses the
+ * same array and leaves its partials there; each call writes every partial it reads, so no
+ * clearing is needed, but calls whose execution overlaps on one GPU (for example on two
+ * streams) race and must be ordered by the caller. */
+size_t orch_attention_noalloc_max_bytes(void);
+int orch_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                  const int32_t* pos, const int32_t* slots, void* out,
+                                  uint32_t M, uint32_t num_heads, uint32_t head_dim,
+                                  uint32_t max_seq, void* stream);
 /* Row argmax of fp32 logits [M, V] (first index of the maximum, as np.argmax;
  * orchard/model.py:244-246). */
 int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, void* stream);

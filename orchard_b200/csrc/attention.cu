@@ -10,6 +10,7 @@
 // are split over several CTAs and their (max, sum, acc) partials are merged by a second
 // small kernel (flash-decoding). Split partials live in a caller-provided workspace.
 #include <algorithm>
+#include <mutex>
 
 #include "orch_common.cuh"
 
@@ -332,4 +333,99 @@ extern "C" int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int
   ORCH_CUDA(launch_k(argmax_rows_kernel, dim3(M), dim3(1024), 0, as_stream(stream), dim3(0, 0, 0), logits,
                      (int)V, (int*)out));
   return check_launch("argmax_rows");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free decode attention.
+//
+// For callers that must not allocate device memory at all: code that runs while a CUDA
+// graph is being captured by someone else, real-time or embedded hosts whose memory is
+// fixed at start-up, and plugin hosts that hand this library only the tensors of the call.
+// The split-position partials live in a file-scope device array instead of a caller
+// workspace. Every GPU that loads the library holds this array until the process exits.
+// ---------------------------------------------------------------------------------------------
+namespace orch {
+
+// 1 MiB of partials: (row, head, split) records of head_dim + 2 floats.
+constexpr size_t kNoAllocScratchFloats = 256 * 1024;
+static __device__ __align__(256) float g_attn_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) uint32_t g_attn_noalloc_check[64];
+
+struct NoAllocState {
+  float* scratch = nullptr;
+  uint32_t* check = nullptr;
+  int sms = 0;
+};
+static NoAllocState g_noalloc[64];
+static std::mutex g_noalloc_mu;
+
+// Host code may not use the arrays' names as addresses; fetch the device addresses once
+// per device, with that device current.
+static int noalloc_setup(int dev, NoAllocState** out) {
+  if (dev < 0 || dev >= 64) return fail(ORCH_ERR_UNSUPPORTED, "attention_decode_noalloc: device index out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocState& st = g_noalloc[dev];
+  if (st.scratch == nullptr) {
+    void* p = nullptr;
+    ORCH_CUDA(cudaGetSymbolAddress(&p, g_attn_scratch));
+    void* c = nullptr;
+    ORCH_CUDA(cudaGetSymbolAddress(&c, g_attn_noalloc_check));
+    int sms = 0;
+    ORCH_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    st.check = static_cast<uint32_t*>(c);
+    st.sms = sms;
+    st.scratch = static_cast<float*>(p);
+  }
+  *out = &st;
+  return ORCH_OK;
+}
+
+static int noalloc_splits(int M, int nh, int max_seq, int sms) {
+  const int pairs = M * nh;
+  int S = std::max(1, (4 * sms + pairs - 1) / pairs);
+  S = std::max(S, (max_seq + kAttnChunk - 1) / kAttnChunk);
+  return std::min(S, std::max(1, (max_seq + 31) / 32));
+}
+
+}  // namespace orch
+
+extern "C" size_t orch_attention_noalloc_max_bytes(void) { return orch::kNoAllocScratchFloats * sizeof(float); }
+
+extern "C" int orch_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                             const int32_t* pos, const int32_t* slots, void* out, uint32_t M,
+                                             uint32_t num_heads, uint32_t head_dim, uint32_t max_seq, void* stream) {
+  if (M == 0) return ORCH_OK;
+  ORCH_REQUIRE(q && k_cache && v_cache && pos && out, "attention_decode_noalloc: null pointer");
+  ORCH_REQUIRE(num_heads > 0 && max_seq > 0, "attention_decode_noalloc: empty shape");
+  ORCH_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
+               "attention_decode_noalloc: head_dim must be 32, 64 or 128");
+  int dev = 0;
+  ORCH_CUDA(cudaGetDevice(&dev));
+  orch::NoAllocState* st = nullptr;
+  int rc = orch::noalloc_setup(dev, &st);
+  if (rc != ORCH_OK) return rc;
+  AttnArgs a;
+  a.q = static_cast<const __half*>(q);
+  a.kc = static_cast<const __half*>(k_cache);
+  a.vc = static_cast<const __half*>(v_cache);
+  a.pos = pos;
+  a.slots = slots;
+  a.out = static_cast<__half*>(out);
+  a.M = (int)M;
+  a.nh = (int)num_heads;
+  a.max_seq = (int)max_seq;
+  a.S = orch::noalloc_splits(a.M, a.nh, a.max_seq, st->sms);
+  a.check = st->check;
+  a.ws = st->scratch;
+  // every split record is written before the combine pass reads it: nothing needs clearing
+  const size_t need = a.S > 1 ? (size_t)M * num_heads * a.S * (head_dim + 2) : 0;
+  if (need > orch::kNoAllocScratchFloats)
+    return fail(ORCH_ERR_UNSUPPORTED, "attention_decode_noalloc: rows x heads x splits exceed the 1 MiB scratch "
+                                      "(use orch_attention_decode with a workspace)");
+  cudaStream_t s = as_stream(stream);
+  switch (head_dim) {
+    case 32: return attn_launch<32>(a, s);
+    case 64: return attn_launch<64>(a, s);
+    default: return attn_launch<128>(a, s);
+  }
 }
