@@ -149,12 +149,14 @@ def time_decode(llm, B, steps, warmup, start_pos):
         eng.pos[:B].add_(1)
     torch.cuda.synchronize(dev)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push(f"timed_decode_b{B}")  # ncu --nvtx-include selects these launches
     s.record()
     for _ in range(steps):
         eng.step(B, logits=True)
         eng.tok_in[:B].copy_(eng.tok_out[:B])
         eng.pos[:B].add_(1)
     e.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     return s.elapsed_time(e) / 1000.0
 
@@ -222,6 +224,41 @@ def kernel_profile(llm, B, pos, reps=3):
             out["other"]["ms"] += ms
             out["other"]["launches"] += n
     return out
+
+
+def time_prefill_lora(llm, reps=3, seqs=8, length=512, rank=16, seed=11):
+    """Config 5: batched prefill of seqs x length random tokens with a rank-16 LoRA on Q and V
+    (A, B ~ N(0, 0.01)); device-timed, tensor-core INT4 GEMMs with M = seqs * length."""
+    import torch
+
+    eng = llm.engine
+    H = eng.cfg.hidden_size
+    g = np.random.default_rng([20261201, 5, seed])
+    per_layer = {li: {m: ((g.standard_normal((H, rank)) * 0.01).astype(np.float32),
+                          (g.standard_normal((rank, H)) * 0.01).astype(np.float32) * 2.0)
+                      for m in ("wq", "wv")} for li in range(eng.cfg.num_hidden_layers)}
+    eng.set_lora(per_layer, rank)
+    prompts = g.integers(0, eng.cfg.vocab_size, (seqs, length)).tolist()
+    llm.prefill(prompts)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        llm.prefill(prompts)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b) / 1000.0)
+    eng.set_lora({}, rank)
+    t = float(np.median(ts))
+    tokens = seqs * length
+    lin = 2.0 * 6_476_005_376 * tokens            # dense-equivalent projection flops (32 layers + lm_head)
+    lin -= 2.0 * 4096 * 32000 * tokens            # prefill computes no logits
+    attn = 4.0 * 32 * 32 * 128 * seqs * length * (length + 1) / 2   # QK^T and PV, causal
+    lora = 2.0 * 32 * 2 * tokens * (H * rank + rank * H)
+    flops = lin + attn + lora
+    return {"workload": f"batched prefill {seqs}x{length} tokens, LoRA r={rank} on Q and V", "ms": round(t * 1e3, 3),
+            "tok_s": round(tokens / t, 1), "tflops": round(flops / t / 1e12, 2), "flops": flops}
 
 
 def cpu_baseline_sample(B, target_s=15.0):
@@ -375,6 +412,10 @@ def run_ours(args):
                    "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"],
                    "api": "Llama.generate_batch_ids (greedy), decode phase",
                    "prefill_s": round(stats["prefill_s"], 2)}
+    pf = time_prefill_lora(llm)
+    peaks_bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    pf["frac_of_bf16_peak"] = round(pf["tflops"] / peaks_bf16, 4)
+    line["prefill_config5"] = pf
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline_sample(B)
         cb.pop("step_s", None)

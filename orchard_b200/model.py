@@ -171,6 +171,33 @@ class DeviceLayer:
 # engine
 # --------------------------------------------------------------------------------------
 
+class RowBuffers:
+    """Activation buffers for up to `rows` token rows: fp32 residual, fp16 GEMM inputs and
+    outputs, per-row token / position / cache slot, LoRA x.A rows and the attention
+    workspace."""
+
+    def __init__(self, rows: int, cfg: "LlamaConfig", max_seq: int, device, logits: bool):
+        H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+        nh, hd = cfg.num_attention_heads, cfg.head_dim
+        self.rows = rows
+        self.x = torch.zeros((rows, H), dtype=torch.float32, device=device)
+        self.xn = torch.zeros((rows, H), dtype=torch.float16, device=device)
+        self.q = torch.zeros((rows, H), dtype=torch.float16, device=device)
+        self.attn = torch.zeros((rows, H), dtype=torch.float16, device=device)
+        self.h = torch.zeros((rows, F), dtype=torch.float16, device=device)
+        self.logits = torch.zeros((rows, V), dtype=torch.float32, device=device) if logits else None
+        self.tok_in = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.tok_out = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.pos = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.slots = torch.arange(rows, dtype=torch.int32, device=device)
+        self.lora_t = torch.zeros((rows, 3 * 64), dtype=torch.float32, device=device)
+        lib = _lib.lib()
+        ms = list(range(1, min(rows, 256) + 1)) + [rows]  # splits only happen for few rows
+        ws = max(lib.orch_attention_workspace_bytes(m, nh, hd, max_seq) for m in ms)
+        self.attn_ws = torch.zeros(max(ws, 16) // 4 + 1, dtype=torch.float32, device=device)
+        self.attn_ws_bytes = ws
+
+
 class DecodeEngine:
     """Device state for up to ``max_batch`` sequences of up to ``max_seq`` positions."""
 
@@ -201,24 +228,20 @@ class DecodeEngine:
         nl, nh, hd = cfg.num_hidden_layers, cfg.num_attention_heads, cfg.head_dim
         self.k_cache = torch.zeros((nl, max_batch, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
-        B = max_batch
-        self.x = torch.zeros((B, H), dtype=torch.float32, device=dev)
-        self.xn = torch.zeros((B, H), dtype=torch.float16, device=dev)
-        self.q = torch.zeros((B, H), dtype=torch.float16, device=dev)
-        self.attn = torch.zeros((B, H), dtype=torch.float16, device=dev)
-        self.h = torch.zeros((B, F), dtype=torch.float16, device=dev)
-        self.logits = torch.zeros((B, V), dtype=torch.float32, device=dev)
-        self.tok_in = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.tok_out = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.slots = torch.arange(B, dtype=torch.int32, device=dev)
         self.lora_r = 0
-        self.lora_t = torch.zeros((B, 3 * 64), dtype=torch.float32, device=dev)
-        ws = max(_lib.lib().orch_attention_workspace_bytes(m, nh, hd, self.max_seq) for m in range(1, B + 1))
-        self.attn_ws = torch.zeros(max(ws, 16) // 4 + 1, dtype=torch.float32, device=dev)
-        self.attn_ws_bytes = ws
+        self.dec = RowBuffers(max_batch, cfg, self.max_seq, dev, logits=True)
+        self.pre: Optional[RowBuffers] = None
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         torch.cuda.synchronize(dev)
+
+    # decode buffers, by name
+    x = property(lambda self: self.dec.x)
+    xn = property(lambda self: self.dec.xn)
+    logits = property(lambda self: self.dec.logits)
+    tok_in = property(lambda self: self.dec.tok_in)
+    tok_out = property(lambda self: self.dec.tok_out)
+    pos = property(lambda self: self.dec.pos)
+    slots = property(lambda self: self.dec.slots)
 
     # -- lora --------------------------------------------------------------------------
     def set_lora(self, per_layer: Dict[int, Dict[str, tuple]], r: int):
@@ -229,47 +252,72 @@ class DecodeEngine:
         self.lora_r = r
         self.graphs.clear()
 
-    def _lora(self, layer, g, x, M, s):
+    def _lora(self, layer, g, x, M, s, bufs):
         if g not in layer.lora:
             return None, None, 0
         a, b, R = layer.lora[g]
         K = a.shape[0]
-        call("orch_lora_xa", ptr(x), ptr(a), ptr(self.lora_t), M, K, R * self.lora_r, s)
-        return ptr(self.lora_t), ptr(b), self.lora_r
+        call("orch_lora_xa", ptr(x), ptr(a), ptr(bufs.lora_t), M, K, R * self.lora_r, s)
+        return ptr(bufs.lora_t), ptr(b), self.lora_r
 
     # -- one step ----------------------------------------------------------------------
-    def run_layers(self, M: int):
-        """All layers for rows [0, M): tokens in tok_in, positions in pos."""
+    def run_layers(self, M: int, bufs: Optional[RowBuffers] = None):
+        """All layers for rows [0, M) of `bufs` (default: the decode buffers): token ids in
+        tok_in, positions in pos, cache slots in slots."""
+        b = bufs if bufs is not None else self.dec
         cfg, s = self.cfg, _stream()
         H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
         nh, hd, eps = cfg.num_attention_heads, cfg.head_dim, cfg.rms_norm_eps
-        call("orch_embed_rows", ptr(self.tok_in), ptr(self.embed), F16 if self.embed.dtype == torch.float16 else F32,
-             ptr(self.x), M, H, V, s)
+        call("orch_embed_rows", ptr(b.tok_in), ptr(self.embed), F16 if self.embed.dtype == torch.float16 else F32,
+             ptr(b.x), M, H, V, s)
         for li, L in enumerate(self.layers):
             kc, vc = self.k_cache[li], self.v_cache[li]
-            call("orch_rmsnorm_ex", ptr(self.x), F32, ptr(L.attn_norm), F32, ptr(self.xn), F16, eps, H, M, s)
-            lt, lb, lr = self._lora(L, "qkv", self.xn, M, s)
-            call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(self.xn), M, H, H, nh, ptr(self.pos),
-                 ptr(self.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(self.q), ptr(kc), ptr(vc),
+            call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.attn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
+            lt, lb, lr = self._lora(L, "qkv", b.xn, M, s, b)
+            call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
+                 ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
                  self.max_seq, lt, lb, lr, s)
-            call("orch_attention_decode", ptr(self.q), ptr(kc), ptr(vc), ptr(self.pos), ptr(self.slots),
-                 ptr(self.attn), M, nh, hd, self.max_seq, ptr(self.attn_ws), self.attn_ws_bytes, s)
-            lt, lb, lr = self._lora(L, "o", self.attn, M, s)
-            call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(self.attn), ptr(self.x), M, H, H, lt, lb, lr, s)
-            call("orch_rmsnorm_ex", ptr(self.x), F32, ptr(L.ffn_norm), F32, ptr(self.xn), F16, eps, H, M, s)
-            lt, lb, lr = self._lora(L, "gu", self.xn, M, s)
-            call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(self.xn), ptr(self.h), M, H, F, lt, lb, lr, s)
-            lt, lb, lr = self._lora(L, "down", self.h, M, s)
-            call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(self.h), ptr(self.x), M, F, H, lt, lb, lr, s)
+            call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
+                 ptr(b.attn), M, nh, hd, self.max_seq, ptr(b.attn_ws), b.attn_ws_bytes, s)
+            lt, lb, lr = self._lora(L, "o", b.attn, M, s, b)
+            call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
+            call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.ffn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
+            lt, lb, lr = self._lora(L, "gu", b.xn, M, s, b)
+            call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
+            lt, lb, lr = self._lora(L, "down", b.h, M, s, b)
+            call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
 
     def run_head(self, M: int):
         """Final RMSNorm, INT4 lm_head (fp32 logits) and argmax into tok_out."""
+        b = self.dec
         cfg, s = self.cfg, _stream()
         H, V = cfg.hidden_size, cfg.vocab_size
-        call("orch_rmsnorm_ex", ptr(self.x), F32, ptr(self.norm), F32, ptr(self.xn), F16, cfg.rms_norm_eps, H, M, s)
-        call("orch_gemm_q4_0_ex", ptr(self.lm_w), ptr(self.lm_s), ptr(self.xn), F16, ptr(self.logits), F32,
+        call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(self.norm), F32, ptr(b.xn), F16, cfg.rms_norm_eps, H, M, s)
+        call("orch_gemm_q4_0_ex", ptr(self.lm_w), ptr(self.lm_s), ptr(b.xn), F16, ptr(b.logits), F32,
              H, V, M, s)
-        call("orch_argmax_rows", ptr(self.logits), M, V, ptr(self.tok_out), s)
+        call("orch_argmax_rows", ptr(b.logits), M, V, ptr(b.tok_out), s)
+
+    def prefill_rows(self, tokens: np.ndarray, positions: np.ndarray, slots: np.ndarray, chunk: int = 4096):
+        """Batched prefill: every prompt token is a row with its own position and cache slot,
+        all layers run once per chunk of rows (rows of one sequence in position order). The
+        projections take the tensor-core GEMM; attention is causal per row (each row attends
+        to positions 0..pos of its slot, written by this or an earlier chunk)."""
+        n = len(tokens)
+        if n == 0:
+            return
+        rows = min(chunk, n)
+        if self.pre is None or self.pre.rows < rows:
+            self.pre = RowBuffers(rows, self.cfg, self.max_seq, self.device, logits=False)
+        b = self.pre
+        t_d = torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device)
+        p_d = torch.as_tensor(np.asarray(positions, np.int32)).to(self.device)
+        s_d = torch.as_tensor(np.asarray(slots, np.int32)).to(self.device)
+        for r0 in range(0, n, rows):
+            m = min(rows, n - r0)
+            b.tok_in[:m].copy_(t_d[r0:r0 + m])
+            b.pos[:m].copy_(p_d[r0:r0 + m])
+            b.slots[:m].copy_(s_d[r0:r0 + m])
+            self.run_layers(m, b)
 
     def kernel_launches_per_step(self, M: int, logits: bool = True) -> int:
         """Kernels of this library one step launches (for reporting)."""
@@ -362,28 +410,22 @@ class Llama:
         out = self.generate_batch_ids(ids, max_tokens=max_tokens, temperature=temperature)
         return [self.tokenizer.decode(seq) for seq in out]
 
-    def prefill(self, prompt_ids: Sequence[Sequence[int]]):
-        """Fills the KV cache with every prompt, one position per step for all rows
-        (rows past their prompt re-feed their last token; those positions are rewritten
-        by decode before they are read)."""
+    def prefill(self, prompt_ids: Sequence[Sequence[int]], chunk: int = 4096):
+        """Fills the KV cache with every prompt in one batched pass per chunk of tokens (the
+        reference feeds them one token at a time through the decode path, orchard/model.py:
+        285-303; the cache contents are the same)."""
         eng = self.engine
         B = len(prompt_ids)
         if B > eng.max_batch:
             raise ValueError(f"batch {B} exceeds max_batch {eng.max_batch}")
         if any(len(p) == 0 for p in prompt_ids):
             raise ValueError("empty prompt")
-        longest = max(len(p) for p in prompt_ids)
-        if longest + 1 > eng.max_seq:
+        if max(len(p) for p in prompt_ids) + 1 > eng.max_seq:
             raise ValueError("prompt longer than the KV cache")
-        eng.reset_cache()
-        toks = np.array([[p[min(i, len(p) - 1)] for p in prompt_ids] for i in range(longest)], np.int32)
-        pos = np.array([[i for _ in prompt_ids] for i in range(longest)], np.int32)
-        toks_d = torch.as_tensor(toks).to(eng.device)
-        pos_d = torch.as_tensor(pos).to(eng.device)
-        for i in range(longest):
-            eng.tok_in[:B].copy_(toks_d[i])
-            eng.pos[:B].copy_(pos_d[i])
-            eng.step(B, logits=False, graph=self.use_graphs)
+        toks = np.concatenate([np.asarray(p, np.int32) for p in prompt_ids])
+        pos = np.concatenate([np.arange(len(p), dtype=np.int32) for p in prompt_ids])
+        slots = np.concatenate([np.full(len(p), b, np.int32) for b, p in enumerate(prompt_ids)])
+        eng.prefill_rows(toks, pos, slots, chunk=chunk)
 
     def generate_batch_ids(self, prompt_ids: Sequence[Sequence[int]], max_tokens: int = 50,
                            temperature: float = 0.7, ignore_eos: bool = False,
