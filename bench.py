@@ -161,6 +161,13 @@ def time_decode(llm, B, steps, warmup, start_pos):
     return s.elapsed_time(e) / 1000.0
 
 
+# INT4 GEMM entry points: argument index of M, K and N, N multiplier, output bytes per element
+QGEMM_ARGS = {"orch_q4_qkv_rope": (3, 4, 5, 3, 2), "orch_q4_linear_swiglu": (4, 5, 6, 2, 1),
+              "orch_q4_linear_resid": (4, 5, 6, 1, 8), "orch_gemm_q4_0_ex": (8, 6, 7, 1, 4),
+              "orch_q4t_qkv_rope": (2, 3, 4, 3, 2), "orch_q4t_linear_swiglu": (3, 4, 5, 2, 1),
+              "orch_q4t_linear_resid": (3, 4, 5, 1, 8), "orch_q4t_gemm": (6, 4, 5, 1, 4)}
+
+
 def kernel_profile(llm, B, pos, reps=3):
     """Per-kernel-family device time of one eager decode step (CUDA events around each
     launch on the launching stream), with each family's algorithmic bytes."""
@@ -196,22 +203,14 @@ def kernel_profile(llm, B, pos, reps=3):
     for name, ev in fam.items():
         ms = sum(a.elapsed_time(b) for a, b, _ in ev) / reps
         n = len(ev) // reps
-        if name in ("orch_q4_qkv_rope", "orch_q4_linear_resid", "orch_q4_linear_swiglu", "orch_gemm_q4_0_ex"):
-            # weights + scales once, activations in, outputs out (fp16 in, fp16/fp32 out)
+        if name in QGEMM_ARGS:
+            # weights + scales once, activations in, outputs out (fp16 in, fp16/fp32 out);
+            # padding of the tiled layout is not counted
             byts = 0
+            im, ik, inn, nmul, out_b = QGEMM_ARGS[name]
             for _, _, args in ev[:n]:
-                if name == "orch_q4_qkv_rope":
-                    Mr, K, N = args[3], args[4], 3 * args[5]
-                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + 2 * Mr * N
-                elif name == "orch_q4_linear_swiglu":
-                    Mr, K, N = args[4], args[5], 2 * args[6]
-                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + Mr * N
-                elif name == "orch_q4_linear_resid":
-                    Mr, K, N = args[4], args[5], args[6]
-                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + 8 * Mr * N
-                else:
-                    K, N, Mr = args[6], args[7], args[8]
-                    byts += N * K // 2 + N * K // 16 + 2 * Mr * K + 4 * Mr * N
+                Mr, K, N = args[im], args[ik], nmul * args[inn]
+                byts += N * K // 2 + N * K // 16 + 2 * Mr * K + out_b * Mr * N
             out["qgemm"] = out.get("qgemm", {"ms": 0.0, "bytes": 0, "launches": 0})
             out["qgemm"]["ms"] += ms
             out["qgemm"]["bytes"] += byts

@@ -164,6 +164,29 @@ int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* x, uint32_t
                      const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
                      void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
                      const float* lora_b, uint32_t lora_r, void* stream);
+/* Tiled INT4 weights (no reference counterpart: the engine's device copy of a weight
+ * packed by orchard/quantizer.py:3-78, re-laid once at load). Rows in tiles of 128, k in
+ * blocks of 256, each (tile, block) one contiguous 18 KB run of packed nibbles and scales,
+ * zero-padded; orch_q4t_bytes() gives the size. orch_q4t_pack converts a reference-layout
+ * weight [N, K/2] + scales [N, K/32]. The orch_q4t_* GEMMs take the tiled buffer in place of
+ * (w, scales) and otherwise match orch_gemm_q4_0_ex (fp16 activations) and the fused
+ * entry points above; they always run on the tcgen05 tensor-core kernel. */
+size_t orch_q4t_bytes(uint32_t N, uint32_t K);
+int orch_q4t_pack(const void* packed, const void* scales, uint32_t N, uint32_t K, void* tiled,
+                  void* stream);
+int orch_q4t_gemm(const void* tiled, const void* in, void* out, int out_dt, uint32_t K, uint32_t N,
+                  uint32_t M, void* stream);
+int orch_q4t_linear_resid(const void* tiled, const void* x, float* resid, uint32_t M, uint32_t K,
+                          uint32_t N, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                          void* stream);
+int orch_q4t_linear_swiglu(const void* tiled13, const void* x, void* h, uint32_t M, uint32_t K,
+                           uint32_t F, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                           void* stream);
+int orch_q4t_qkv_rope(const void* tiled_qkv, const void* x, uint32_t M, uint32_t K, uint32_t H,
+                      uint32_t num_heads, const int32_t* pos, const int32_t* slots,
+                      const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
+                      void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
+                      const float* lora_b, uint32_t lora_r, void* stream);
 /* Decode attention over the device KV cache (orchard/model.py:117-137): for each row m and
  * head h, softmax(q.K[0..pos] / sqrt(hd)) . V[0..pos]. q, out fp16 [M, num_heads*head_dim].
  * Long rows are split over positions; the split partials go to `workspace` (fp32,

@@ -31,25 +31,9 @@ struct AttnArgs {
   uint32_t* check;
 };
 
-// VPL consecutive halves (VPL = 1, 2, 4) as floats, one load.
-template <int VPL>
-__device__ __forceinline__ void load_v(const __half* p, float (&f)[VPL]) {
-  if (VPL == 4) {
-    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
-    const float2 a = __half22float2(bits_h2(raw.x)), b = __half22float2(bits_h2(raw.y));
-    f[0] = a.x; f[1] = a.y; f[2 % VPL] = b.x; f[3 % VPL] = b.y;
-  } else if (VPL == 2) {
-    const float2 a = __half22float2(bits_h2(__ldg(reinterpret_cast<const unsigned int*>(p))));
-    f[0] = a.x; f[1 % VPL] = a.y;
-  } else {
-    f[0] = __half2float(p[0]);
-  }
-}
-
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
-  constexpr int VPL = HD / 32;  // dims per lane in the P.V pass
-  __shared__ float qs[HD];
+  __shared__ __align__(16) float qs[HD];
   __shared__ float sc[kAttnChunk];
   __shared__ float red[32];
   __shared__ float accs[kAttnThreads / 32][HD];
@@ -78,21 +62,29 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     qs[d] = __half2float(a.q[(size_t)m * a.nh * HD + h * HD + d]) * scale;
   __syncthreads();
 
-  // pass 1: one position per thread, full-row dot product (row = HD halves)
+  // pass 1: one position per thread, full-row dot product (row = HD halves); the whole
+  // row is requested before it is used, and q comes from shared memory as float4
+  const float4* q4 = reinterpret_cast<const float4*>(qs);
   float lmax = -INFINITY;
   for (int t = p0 + threadIdx.x; t < p1; t += kAttnThreads) {
-    const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)t * HD);
+    const __half* kr = K + (size_t)t * HD;
+    uint4 raw[HD / 8];
+#pragma unroll
+    for (int v = 0; v < HD / 8; ++v) raw[v] = ld_stream16(kr + v * 8);
     float s = 0.f;
 #pragma unroll
     for (int v = 0; v < HD / 8; ++v) {
-      const uint4 raw = __ldg(kr + v);
-      const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(hp[e]);
-        s = fmaf(f.x, qs[v * 8 + 2 * e], s);
-        s = fmaf(f.y, qs[v * 8 + 2 * e + 1], s);
-      }
+      const float4 qa = q4[2 * v], qb = q4[2 * v + 1];
+      const float2 f0 = __half22float2(bits_h2(raw[v].x)), f1 = __half22float2(bits_h2(raw[v].y));
+      const float2 f2 = __half22float2(bits_h2(raw[v].z)), f3 = __half22float2(bits_h2(raw[v].w));
+      s = fmaf(f0.x, qa.x, s);
+      s = fmaf(f0.y, qa.y, s);
+      s = fmaf(f1.x, qa.z, s);
+      s = fmaf(f1.y, qa.w, s);
+      s = fmaf(f2.x, qb.x, s);
+      s = fmaf(f2.y, qb.y, s);
+      s = fmaf(f3.x, qb.z, s);
+      s = fmaf(f3.y, qb.w, s);
     }
     sc[t - p0] = s;
     lmax = fmaxf(lmax, s);
@@ -106,35 +98,42 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   }
   const float sum = block_sum(lsum, red);  // contains __syncthreads: sc[] complete
 
-  // pass 2: warp w takes positions w, w+4, ...; lane owns VPL consecutive dims
+  // pass 2: LPR lanes cover one position row in 16-byte pieces, so a warp load instruction
+  // reads RPW whole rows; U such loads per lane are in flight before any is used
+  constexpr int LPR = HD / 8, RPW = 32 / LPR, NW = kAttnThreads / 32, STR = NW * RPW, U = 8;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float acc[VPL];
+  const int sub = lane / LPR, ci = lane - sub * LPR;
+  float acc[8];
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) acc[i] = 0.f;
-  int t = p0 + warp;
-  for (; t + 3 * (kAttnThreads / 32) < p1; t += 4 * (kAttnThreads / 32)) {
-    float w[4];
-    float vv[4][VPL];
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  auto fma8 = [&](const uint4& raw, float w) {
+    const float2 f0 = __half22float2(bits_h2(raw.x)), f1 = __half22float2(bits_h2(raw.y));
+    const float2 f2 = __half22float2(bits_h2(raw.z)), f3 = __half22float2(bits_h2(raw.w));
+    acc[0] = fmaf(w, f0.x, acc[0]);
+    acc[1] = fmaf(w, f0.y, acc[1]);
+    acc[2] = fmaf(w, f1.x, acc[2]);
+    acc[3] = fmaf(w, f1.y, acc[3]);
+    acc[4] = fmaf(w, f2.x, acc[4]);
+    acc[5] = fmaf(w, f2.y, acc[5]);
+    acc[6] = fmaf(w, f3.x, acc[6]);
+    acc[7] = fmaf(w, f3.y, acc[7]);
+  };
+  int t = p0 + warp * RPW + sub;
+  for (; t + (U - 1) * STR < p1; t += U * STR) {
+    uint4 raw[U];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int tq = t + q * (kAttnThreads / 32);
-      w[q] = sc[tq - p0];
-      load_v<VPL>(V + (size_t)tq * HD + lane * VPL, vv[q]);
-    }
+    for (int u = 0; u < U; ++u) raw[u] = ld_stream16(V + (size_t)(t + u * STR) * HD + ci * 8);
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) acc[i] = fmaf(w[q], vv[q][i], acc[i]);
+    for (int u = 0; u < U; ++u) fma8(raw[u], sc[t + u * STR - p0]);
   }
-  for (; t < p1; t += kAttnThreads / 32) {
-    const float w = sc[t - p0];
-    float vv[VPL];
-    load_v<VPL>(V + (size_t)t * HD + lane * VPL, vv);
+  for (; t < p1; t += STR) fma8(ld_stream16(V + (size_t)t * HD + ci * 8), sc[t - p0]);
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) acc[i] = fmaf(w, vv[i], acc[i]);
-  }
+  for (int o = LPR; o < 32; o <<= 1)
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) accs[warp][lane * VPL + i] = acc[i];
+    for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  if (sub == 0)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) accs[warp][ci * 8 + i] = acc[i];
   __syncthreads();
   for (int d = threadIdx.x; d < HD; d += kAttnThreads) {
     float v = 0.f;

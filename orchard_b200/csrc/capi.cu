@@ -265,14 +265,24 @@ static int set_lora(QArgs& a, const float* t, const float* b, uint32_t r) {
   return ORCH_OK;
 }
 
-extern "C" int orch_q4_linear_resid(const void* w, const void* scales, const void* x, float* resid,
-                                    uint32_t M, uint32_t K, uint32_t N, const float* lora_t,
-                                    const float* lora_b, uint32_t lora_r, void* stream) {
+// Weights of the fused entry points: reference layout (w + scales) or tiled (scales null).
+static int check_q4w(const void* w, const void* s, const void* x, uint32_t K, bool tiled) {
+  if (!tiled) return check_wx(w, s, x, K);
+  ORCH_REQUIRE(w && x, "tiled INT4 GEMM: null pointer");
+  if (K == 0 || K % 32 != 0) return fail(ORCH_ERR_UNSUPPORTED, "tiled INT4 GEMM: K must be a positive multiple of 32");
+  ORCH_REQUIRE(((uintptr_t)w & 15) == 0 && ((uintptr_t)x & 15) == 0, "tiled INT4 GEMM: buffers must be 16-byte aligned");
+  return ORCH_OK;
+}
+
+static int linear_resid(const void* w, const void* scales, bool tiled, const void* x, float* resid, uint32_t M,
+                        uint32_t K, uint32_t N, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                        void* stream) {
   if (M == 0 || N == 0) return ORCH_OK;
-  int rc = check_wx(w, scales, x, K);
+  int rc = check_q4w(w, scales, x, K, tiled);
   if (rc) return rc;
   ORCH_REQUIRE(resid, "q4_linear_resid: null residual");
   QArgs a = base_args(w, scales, x, ORCH_F16, M, K, N);
+  a.tiled = tiled;
   a.out = resid;
   a.out_f32 = 1;
   a.ldo = (int)N;
@@ -280,27 +290,26 @@ extern "C" int orch_q4_linear_resid(const void* w, const void* scales, const voi
   return qgemm_run<W_Q4, EPI_RESID>(a, as_stream(stream));
 }
 
-extern "C" int orch_q4_linear_swiglu(const void* w13, const void* s13, const void* x, void* h, uint32_t M,
-                                     uint32_t K, uint32_t F, const float* lora_t, const float* lora_b,
-                                     uint32_t lora_r, void* stream) {
+static int linear_swiglu(const void* w13, const void* s13, bool tiled, const void* x, void* h, uint32_t M, uint32_t K,
+                         uint32_t F, const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream) {
   if (M == 0 || F == 0) return ORCH_OK;
-  int rc = check_wx(w13, s13, x, K);
+  int rc = check_q4w(w13, s13, x, K, tiled);
   if (rc) return rc;
   ORCH_REQUIRE(h, "q4_linear_swiglu: null output");
   if (F % 16 != 0) return fail(ORCH_ERR_UNSUPPORTED, "q4_linear_swiglu: F must be a multiple of 16");
   QArgs a = base_args(w13, s13, x, ORCH_F16, M, K, 2 * F);
+  a.tiled = tiled;
   a.out = h;
   if ((rc = set_lora(a, lora_t, lora_b, lora_r))) return rc;
   return qgemm_run<W_Q4, EPI_SWIGLU>(a, as_stream(stream));
 }
 
-extern "C" int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* x, uint32_t M, uint32_t K,
-                                uint32_t H, uint32_t num_heads, const int32_t* pos, const int32_t* slots,
-                                const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
-                                void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
-                                const float* lora_b, uint32_t lora_r, void* stream) {
+static int qkv_rope(const void* wqkv, const void* sqkv, bool tiled, const void* x, uint32_t M, uint32_t K, uint32_t H,
+                    uint32_t num_heads, const int32_t* pos, const int32_t* slots, const float* cos_tab,
+                    const float* sin_tab, uint32_t max_pos, void* q_out, void* k_cache, void* v_cache,
+                    uint32_t max_seq, const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream) {
   if (M == 0) return ORCH_OK;
-  int rc = check_wx(wqkv, sqkv, x, K);
+  int rc = check_q4w(wqkv, sqkv, x, K, tiled);
   if (rc) return rc;
   ORCH_REQUIRE(pos && cos_tab && sin_tab && q_out && k_cache && v_cache, "q4_qkv_rope: null pointer");
   ORCH_REQUIRE(num_heads > 0 && H % num_heads == 0, "q4_qkv_rope: H must be a multiple of num_heads");
@@ -308,6 +317,7 @@ extern "C" int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* 
   ORCH_REQUIRE(hd % 2 == 0, "q4_qkv_rope: head_dim must be even");
   ORCH_REQUIRE(max_seq > 0 && max_pos > 0, "q4_qkv_rope: empty cache");
   QArgs a = base_args(wqkv, sqkv, x, ORCH_F16, M, K, 3 * H);
+  a.tiled = tiled;
   a.out = q_out;
   a.H = (int)H;
   a.nh = (int)num_heads;
@@ -322,4 +332,62 @@ extern "C" int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* 
   a.vc = static_cast<__half*>(v_cache);
   if ((rc = set_lora(a, lora_t, lora_b, lora_r))) return rc;
   return qgemm_run<W_Q4, EPI_QKV>(a, as_stream(stream));
+}
+
+extern "C" int orch_q4_linear_resid(const void* w, const void* scales, const void* x, float* resid,
+                                    uint32_t M, uint32_t K, uint32_t N, const float* lora_t,
+                                    const float* lora_b, uint32_t lora_r, void* stream) {
+  return linear_resid(w, scales, false, x, resid, M, K, N, lora_t, lora_b, lora_r, stream);
+}
+
+extern "C" int orch_q4_linear_swiglu(const void* w13, const void* s13, const void* x, void* h, uint32_t M,
+                                     uint32_t K, uint32_t F, const float* lora_t, const float* lora_b,
+                                     uint32_t lora_r, void* stream) {
+  return linear_swiglu(w13, s13, false, x, h, M, K, F, lora_t, lora_b, lora_r, stream);
+}
+
+extern "C" int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* x, uint32_t M, uint32_t K,
+                                uint32_t H, uint32_t num_heads, const int32_t* pos, const int32_t* slots,
+                                const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
+                                void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
+                                const float* lora_b, uint32_t lora_r, void* stream) {
+  return qkv_rope(wqkv, sqkv, false, x, M, K, H, num_heads, pos, slots, cos_tab, sin_tab, max_pos, q_out, k_cache,
+                  v_cache, max_seq, lora_t, lora_b, lora_r, stream);
+}
+
+// ---- tiled-layout forms (weights re-laid by orch_q4t_pack) ----------------------------------
+extern "C" int orch_q4t_gemm(const void* tiled, const void* in, void* out, int out_dt, uint32_t K, uint32_t N,
+                             uint32_t M, void* stream) {
+  if (M == 0 || N == 0) return ORCH_OK;
+  int rc = check_q4w(tiled, nullptr, in, K, true);
+  if (rc) return rc;
+  ORCH_REQUIRE(out, "q4t_gemm: null output");
+  ORCH_REQUIRE(out_dt == ORCH_F16 || out_dt == ORCH_F32, "q4t_gemm: bad dtype");
+  QArgs a = base_args(tiled, nullptr, in, ORCH_F16, M, K, N);
+  a.tiled = 1;
+  a.out = out;
+  a.out_f32 = out_dt == ORCH_F32;
+  a.ldo = (int)N;
+  return qgemm_run<W_Q4, EPI_STORE>(a, as_stream(stream));
+}
+
+extern "C" int orch_q4t_linear_resid(const void* tiled, const void* x, float* resid, uint32_t M, uint32_t K,
+                                     uint32_t N, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                                     void* stream) {
+  return linear_resid(tiled, nullptr, true, x, resid, M, K, N, lora_t, lora_b, lora_r, stream);
+}
+
+extern "C" int orch_q4t_linear_swiglu(const void* tiled13, const void* x, void* h, uint32_t M, uint32_t K,
+                                      uint32_t F, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                                      void* stream) {
+  return linear_swiglu(tiled13, nullptr, true, x, h, M, K, F, lora_t, lora_b, lora_r, stream);
+}
+
+extern "C" int orch_q4t_qkv_rope(const void* tiled_qkv, const void* x, uint32_t M, uint32_t K, uint32_t H,
+                                 uint32_t num_heads, const int32_t* pos, const int32_t* slots, const float* cos_tab,
+                                 const float* sin_tab, uint32_t max_pos, void* q_out, void* k_cache, void* v_cache,
+                                 uint32_t max_seq, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                                 void* stream) {
+  return qkv_rope(tiled_qkv, nullptr, true, x, M, K, H, num_heads, pos, slots, cos_tab, sin_tab, max_pos, q_out,
+                  k_cache, v_cache, max_seq, lora_t, lora_b, lora_r, stream);
 }

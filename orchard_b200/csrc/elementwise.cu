@@ -28,6 +28,65 @@ __global__ void rmsnorm_kernel(const TI* in, const TW* w, TO* out, float eps, in
   for (int i = threadIdx.x; i < N; i += blockDim.x) o[i] = from_f32<TO>(to_f32(r[i]) * inv * to_f32(w[i]));
 }
 
+// Vectorised form for N % 4 == 0, N <= 4 * V * blockDim.x: each thread holds its V
+// four-element pieces of the row in registers, so the row is read once and every load is
+// in flight at the same time (the generic loop above waits one memory latency per element
+// it reads). The gamma pieces do not depend on the previous kernel and are requested first.
+template <typename T> __device__ __forceinline__ float4 ld4(const T* p);
+template <> __device__ __forceinline__ float4 ld4<float>(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+template <> __device__ __forceinline__ float4 ld4<__half>(const __half* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(bits_h2(u.x)), b = __half22float2(bits_h2(u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+template <typename T> __device__ __forceinline__ void st4(T* p, float4 v);
+template <> __device__ __forceinline__ void st4<float>(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+template <> __device__ __forceinline__ void st4<__half>(__half* p, float4 v) {
+  uint2 u;
+  u.x = h2_bits(__floats2half2_rn(v.x, v.y));
+  u.y = h2_bits(__floats2half2_rn(v.z, v.w));
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <typename TI, typename TW, typename TO, int V>
+__global__ void rmsnorm_vec_kernel(const TI* in, const TW* w, TO* out, float eps, int N) {
+  __shared__ float red[32];
+  pdl_trigger();
+  float4 g[V], v[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 4;
+    g[j] = i < N ? ld4(w + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  pdl_wait();
+  const TI* r = in + (size_t)blockIdx.x * N;
+  TO* o = out + (size_t)blockIdx.x * N;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 4;
+    v[j] = i < N ? ld4(r + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    ss = fmaf(v[j].x, v[j].x, ss);
+    ss = fmaf(v[j].y, v[j].y, ss);
+    ss = fmaf(v[j].z, v[j].z, ss);
+    ss = fmaf(v[j].w, v[j].w, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / (float)N + eps);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 4;
+    if (i < N)
+      st4(o + i, make_float4(v[j].x * inv * g[j].x, v[j].y * inv * g[j].y, v[j].z * inv * g[j].z,
+                             v[j].w * inv * g[j].w));
+  }
+}
+
 // ---- RoPE: in/out [rows, heads, hd], cos/sin [rows, hd/2] ---------------------------------
 template <typename TI, typename TT, typename TO>
 __global__ void rope_kernel(const TI* in, const TT* cs, const TT* sn, TO* out, int hd, int heads,
@@ -152,9 +211,20 @@ extern "C" int orch_rmsnorm_ex(const void* in, int in_dt, const void* weight, in
   ORCH_REQUIRE(DT_OK(in_dt) && DT_OK(w_dt) && DT_OK(out_dt), "rmsnorm: bad dtype");
   cudaStream_t st = as_stream(stream);
   const int th = N >= 1024 ? 256 : 128;
-#define RMS_CASE(TI, TW, TO)                                                                   \
-  ORCH_CUDA(launch_k(rmsnorm_kernel<TI, TW, TO>, dim3(count), dim3(th), 0, st, dim3(0, 0, 0), (const TI*)in, \
-                     (const TW*)weight, (TO*)out, eps, (int)N))
+  // vector path: 16-byte (fp32) / 8-byte (fp16) aligned rows of at most 4 * 8 * 256 elements
+  const bool vec = (N % 4) == 0 && N <= 8192 && ((uintptr_t)in & 15) == 0 && ((uintptr_t)weight & 15) == 0 &&
+                   ((uintptr_t)out & 15) == 0;
+  const bool v4 = N <= 4096;
+#define RMS_CASE(TI, TW, TO)                                                                                     \
+  if (vec && v4)                                                                                                 \
+    ORCH_CUDA(launch_k(rmsnorm_vec_kernel<TI, TW, TO, 4>, dim3(count), dim3(256), 0, st, dim3(0, 0, 0),          \
+                       (const TI*)in, (const TW*)weight, (TO*)out, eps, (int)N));                                 \
+  else if (vec)                                                                                                  \
+    ORCH_CUDA(launch_k(rmsnorm_vec_kernel<TI, TW, TO, 8>, dim3(count), dim3(256), 0, st, dim3(0, 0, 0),          \
+                       (const TI*)in, (const TW*)weight, (TO*)out, eps, (int)N));                                 \
+  else                                                                                                           \
+    ORCH_CUDA(launch_k(rmsnorm_kernel<TI, TW, TO>, dim3(count), dim3(th), 0, st, dim3(0, 0, 0), (const TI*)in,   \
+                       (const TW*)weight, (TO*)out, eps, (int)N))
   const int key = in_dt * 4 + w_dt * 2 + out_dt;
   switch (key) {
     case 0: RMS_CASE(float, float, float); break;

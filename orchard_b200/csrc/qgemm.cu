@@ -246,10 +246,13 @@ __global__ void __launch_bounds__(kThreads) qgemm_kernel(const QArgs a) {
     for (int nt = 0; nt < NT; ++nt) {
       const int n0 = nt * 8 + 2 * c;
       if (n0 < Mp) {  // Mp is a multiple of 4, so n0 + 1 < Mp too
-        *reinterpret_cast<float2*>(epi_dest<EPI, ROWS>(cl, recv, Mp, KS, ks, rl, n0)) =
-            make_float2(acc[mt][nt][0], acc[mt][nt][1]);
-        *reinterpret_cast<float2*>(epi_dest<EPI, ROWS>(cl, recv, Mp, KS, ks, rl + 8, n0)) =
-            make_float2(acc[mt][nt][2], acc[mt][nt][3]);
+        const int pitch = epi_pitch<EPI, ROWS>(KS);
+        float* d0 = epi_dest<EPI, ROWS>(cl, recv, Mp, KS, ks, rl, n0);
+        float* d1 = epi_dest<EPI, ROWS>(cl, recv, Mp, KS, ks, rl + 8, n0);
+        d0[0] = acc[mt][nt][0];
+        d0[pitch] = acc[mt][nt][1];
+        d1[0] = acc[mt][nt][2];
+        d1[pitch] = acc[mt][nt][3];
       }
     }
   }
@@ -298,6 +301,13 @@ template <int WF, int EPI>
 int qgemm_run(QArgs a, cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0) return ORCH_OK;
   if (a.K <= 0 || (a.K % 32) != 0) return fail(ORCH_ERR_UNSUPPORTED, "K must be a positive multiple of 32");
+  if (a.tiled) {  // tiled INT4 weights: tensor-core path for every M
+    if (WF != W_Q4) return fail(ORCH_ERR_INVALID, "tiled weights are INT4 only");
+    const int rc = tc_qgemm_run<EPI>(a, st);
+    if (rc == ORCH_ERR_UNSUPPORTED)
+      return fail(ORCH_ERR_UNSUPPORTED, "tiled INT4 GEMM: needs fp16 activations and 16-byte aligned buffers");
+    return rc;
+  }
   if (WF == W_Q4 && !a.x_f32 && tc_min_m() > 0 && a.M >= (int)tc_min_m()) {
     const int rc = tc_qgemm_run<EPI>(a, st);
     if (rc != ORCH_ERR_UNSUPPORTED) return rc;

@@ -10,6 +10,25 @@ namespace orch {
 enum { W_Q4 = 0, W_Q8G = 1, W_Q8PC = 2 };
 enum { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV = 3 };
 
+// Tiled INT4 weight layout: the engine's device copy of a packed [N, K/2] + [N, K/32]
+// weight, re-laid once at load so that the tensor-core GEMM streams every CTA's weights
+// as one contiguous run (row-major rows read 32 bytes at a time leave HBM activation-bound).
+// Rows come in tiles of 128, k in blocks of 256 (N and K are padded with zero weights:
+// nibble 8, scale 0). Block (tile t, block b) sits at byte (t * nblk + b) * kQ4tBlockBytes:
+//   4 stages of 64 k, each [2 halves of 32 k][128 rows][16 bytes];
+//   then the block's scales [8 groups][128 rows] fp16.
+// Inside each 32-bit word the nibbles of k0..k7 are stored in the order
+// k0 k2 k4 k6 k1 k3 k5 k7 (low nibble first), so the magic-exponent extraction yields
+// (k0,k1) (k2,k3) (k4,k5) (k6,k7) pairs directly.
+constexpr int kQ4tRows = 128;
+constexpr int kQ4tBlockK = 256;
+constexpr int kQ4tStageBytes = 4096;
+constexpr int kQ4tScaleBytes = 2048;
+constexpr int kQ4tBlockBytes = 4 * kQ4tStageBytes + kQ4tScaleBytes;
+inline size_t q4t_bytes(uint32_t N, uint32_t K) {
+  return (size_t)((N + kQ4tRows - 1) / kQ4tRows) * ((K + kQ4tBlockK - 1) / kQ4tBlockK) * kQ4tBlockBytes;
+}
+
 struct QArgs {
   const uint8_t* w;   // packed weights [N, K/2] (INT4) or [N, K] (INT8)
   const __half* s;    // scales [N, K/32] or [N] (per channel)
@@ -33,6 +52,7 @@ struct QArgs {
   const float* lora_b;
   int lora_r;
   uint32_t* check;
+  int tiled;          // w is in the tiled INT4 layout (s unused); tensor-core path only
 };
 
 template <int WF, int EPI>
@@ -63,17 +83,19 @@ __device__ __forceinline__ float lora_delta_r(const QArgs& a, int n, int reg, in
 // (QKV) or the gate and up rows of one output (SWIGLU, rows 32b+i and 32b+16+i). The ROWS/E
 // item rows of a tile are owned in equal contiguous blocks of IRL = ROWS/E/KS by the KS
 // CTAs of the cluster. Each CTA pushes its partial sums into the owners' receive buffers
-// with distributed-shared-memory vector stores (no remote loads); after one cluster barrier
-// every owner sums its KS slices locally and runs the epilogue, consecutive threads on
-// consecutive rows. Receive buffer of an owner: [src][irl][e][Mp] floats, Mp = M rounded
-// up to 4 (ROWS * Mp floats in total).
+// with distributed-shared-memory stores (no remote loads); after one cluster barrier every
+// owner sums its KS slices locally and runs the epilogue, consecutive threads on
+// consecutive rows. Receive buffer of an owner: [src][e][n][irl] floats, the row index
+// fastest with a pitch of IRL + 1 per activation row n (n < Mp, M rounded up to 4), so the
+// owner's sum loop and a warp pushing 32 consecutive rows of one n touch 32 consecutive
+// words (no bank conflicts). Size Mp * (ROWS + E * KS) floats <= Mp * (ROWS + 16).
 template <int EPI>
 __host__ __device__ constexpr int epi_elems() { return (EPI == EPI_QKV || EPI == EPI_SWIGLU) ? 2 : 1; }
 
 __host__ __device__ __forceinline__ int epi_mp(int M) { return (M + 3) & ~3; }
 
 template <int ROWS>
-__host__ __device__ __forceinline__ int epi_recv_floats(int M) { return ROWS * epi_mp(M); }
+__host__ __device__ __forceinline__ int epi_recv_floats(int M) { return (ROWS + 16) * epi_mp(M); }
 
 template <int EPI>
 __device__ __forceinline__ int epi_item_row(int rl, int& e) {
@@ -90,7 +112,12 @@ __device__ __forceinline__ int epi_item_row(int rl, int& e) {
   return rl;
 }
 
-// Destination of the partial sums of tile row `rl` for activation rows n..n+W-1 (n % W == 0).
+// Distance in floats between the partials of activation rows n and n + 1.
+template <int EPI, int ROWS>
+__device__ __forceinline__ int epi_pitch(int KS) { return ROWS / epi_elems<EPI>() / KS + 1; }
+
+// Destination of the partial sum of tile row `rl` for activation row n; the partial of row
+// n + j goes to the returned pointer + j * epi_pitch.
 template <int EPI, int ROWS>
 __device__ __forceinline__ float* epi_dest(cg::cluster_group& cl, float* recv, int Mp, int KS, int ks, int rl,
                                            int n) {
@@ -101,7 +128,7 @@ __device__ __forceinline__ float* epi_dest(cg::cluster_group& cl, float* recv, i
   const int irow = epi_item_row<EPI>(rl, e);
   const int q = irow / IRL, irl = irow - q * IRL;
   float* base = (q == ks) ? recv : cl.map_shared_rank(recv, q);
-  return base + ((ks * IRL + irl) * E + e) * Mp + n;
+  return base + ((ks * E + e) * Mp + n) * (IRL + 1) + irl;
 }
 
 // After every CTA of the cluster pushed its partials: the cluster barrier, then the sums and
@@ -121,7 +148,7 @@ __device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, 
   const int items = IRL * a.M;
   auto total = [&](int irl, int n, int e) {
     float v = 0.f;
-    for (int r = 0; r < KS; ++r) v += recv[((r * IRL + irl) * E + e) * Mp + n];
+    for (int r = 0; r < KS; ++r) v += recv[((r * E + e) * Mp + n) * (IRL + 1) + irl];
     return v;
   };
   if (EPI == EPI_STORE || EPI == EPI_RESID) {

@@ -6,7 +6,7 @@
 // (__fdiv_rn/__fadd_rn, so no contraction changes a bit); low nibble = even k.
 // INT8 (src/main.cpp:35-64): scale = fp16_rne(max|w| / 127), zero -> 1.0,
 // q = round-half-away(w / scale); group 32 or one group per output row.
-#include "orch_common.cuh"
+#include "qgemm.cuh"
 
 namespace orch {
 
@@ -44,7 +44,8 @@ __device__ __forceinline__ void load32<__half>(const __half* p, float (&v)[32]) 
 
 template <typename T>
 __global__ void quant_q4_kernel(const T* w, uint8_t* packed, __half* scales, size_t groups) {
-  pdl_trigger();
+  // No early griddepcontrol.launch_dependents here: the GEMMs start streaming weights
+  // before their own griddepcontrol.wait, so a packer releases dependents only on exit.
   pdl_wait();
   for (size_t gi = blockIdx.x * (size_t)blockDim.x + threadIdx.x; gi < groups;
        gi += (size_t)gridDim.x * blockDim.x) {
@@ -72,8 +73,7 @@ __global__ void quant_q4_kernel(const T* w, uint8_t* packed, __half* scales, siz
 // One group of `gs` consecutive weights per warp (gs = 32 or the row length).
 template <typename T>
 __global__ void quant_q8_kernel(const T* w, int8_t* q, __half* scales, size_t groups, int gs) {
-  pdl_trigger();
-  pdl_wait();
+  pdl_wait();  // releases dependents only on exit (see quant_q4_kernel)
   const int lane = threadIdx.x & 31;
   const size_t warp = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
   const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -91,6 +91,48 @@ __global__ void quant_q8_kernel(const T* w, int8_t* q, __half* scales, size_t gr
       q[gi * gs + i] = (int8_t)(int)r;
     }
     if (lane == 0) scales[gi] = sh;
+  }
+}
+
+// Standard packed INT4 -> tiled layout (qgemm.cuh). One thread per (tile, block, row):
+// the row's 128 packed bytes of the block (8 x 16) and its 8 scales.
+__device__ __forceinline__ uint32_t q4t_word(uint32_t w) {
+  // nibble p of the result is nibble {0,2,4,6,1,3,5,7}[p] of w
+  uint32_t o = 0;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    const int q = (p < 4) ? 2 * p : 2 * (p - 4) + 1;
+    o |= ((w >> (4 * q)) & 0xFu) << (4 * p);
+  }
+  return o;
+}
+
+__global__ void q4t_pack_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ sc, uint8_t* __restrict__ out,
+                                int N, int K, int nblk, size_t units) {
+  pdl_wait();
+  const int G = K / 32;
+  for (size_t u = blockIdx.x * (size_t)blockDim.x + threadIdx.x; u < units; u += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(u % kQ4tRows);
+    const size_t tb = u / kQ4tRows;  // tile * nblk + block
+    const int b = (int)(tb % nblk);
+    const int row = (int)(tb / nblk) * kQ4tRows + r;
+    uint8_t* blk = out + tb * kQ4tBlockBytes;
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {  // 32-k halves of the block: stage j/2, half j%2
+      const int g = b * 8 + j;      // scale group
+      uint4 v = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+      __half s = __float2half(0.f);
+      if (row < N && g < G) {
+        v = *reinterpret_cast<const uint4*>(w + (size_t)row * (K / 2) + (size_t)g * 16);
+        s = sc[(size_t)row * G + g];
+        v.x = q4t_word(v.x);
+        v.y = q4t_word(v.y);
+        v.z = q4t_word(v.z);
+        v.w = q4t_word(v.w);
+      }
+      *reinterpret_cast<uint4*>(blk + (j >> 1) * kQ4tStageBytes + (j & 1) * 2048 + r * 16) = v;
+      reinterpret_cast<__half*>(blk + 4 * kQ4tStageBytes)[j * kQ4tRows + r] = s;
+    }
   }
 }
 
@@ -149,4 +191,20 @@ extern "C" int orch_quantize_q8_pc(const void* w, int w_dt, void* q, void* scale
   if (N == 0 || K == 0) return ORCH_OK;
   ORCH_REQUIRE(w && q && scales, "quantize_q8_pc: null pointer");
   return quant_q8(w, w_dt, q, scales, (size_t)N, (int)K, stream);
+}
+
+extern "C" size_t orch_q4t_bytes(uint32_t N, uint32_t K) { return (N == 0 || K == 0) ? 0 : q4t_bytes(N, K); }
+
+extern "C" int orch_q4t_pack(const void* packed, const void* scales, uint32_t N, uint32_t K, void* tiled,
+                             void* stream) {
+  if (N == 0 || K == 0) return ORCH_OK;
+  ORCH_REQUIRE(packed && scales && tiled, "q4t_pack: null pointer");
+  ORCH_REQUIRE(K % 32 == 0, "q4t_pack: K must be divisible by the group size 32");
+  ORCH_REQUIRE(((uintptr_t)packed & 15) == 0 && ((uintptr_t)tiled & 15) == 0,
+               "q4t_pack: buffers must be 16-byte aligned");
+  const int nblk = (int)((K + kQ4tBlockK - 1) / kQ4tBlockK);
+  const size_t units = (size_t)((N + kQ4tRows - 1) / kQ4tRows) * nblk * kQ4tRows;
+  ORCH_CUDA(launch_k(q4t_pack_kernel, dim3(qgrid(units, 128)), dim3(128), 0, as_stream(stream), dim3(0, 0, 0),
+                     (const uint8_t*)packed, (const __half*)scales, (uint8_t*)tiled, (int)N, (int)K, nblk, units));
+  return check_launch("q4t_pack");
 }

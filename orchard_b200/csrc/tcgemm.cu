@@ -1,21 +1,25 @@
-// INT4 dequant GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), for M >= 16
+// INT4 dequant GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), for M >= 17
 // activation rows: batched decode (M = 16..256) and prefill (M = thousands of tokens).
 //
 // Replaces the reference's batched kernel (orchard/kernels/gemm_int4.metal:10-68, one
 // thread per output, weights re-read per row) for the same packed format
 // (orchard/quantizer.py:3-78).
 //
-// D[128 weight rows, NT tokens] (fp32, TMEM) += A[128, 16] . B[NT, 16]^T per MMA, with
-//  * A = dequantised weights: thread t of the CTA owns weight row R0 + t, streams its
-//    packed nibbles (32 bytes per 64-k stage, four stages ahead in registers), turns them
-//    into fp16 (q - 8) * scale with the magic-exponent trick and stores them into a
-//    128B-swizzled K-major shared-memory tile (the canonical UMMA layout);
-//  * B = activations [tokens, K] fp16, loaded by TMA (SWIZZLE_128B; rows past M and k
-//    past K read as zero) into a four-stage ring guarded by mbarriers;
-//  * one thread issues tcgen05.mma.kind::f16 and tcgen05.commit releases each stage.
-// After the K loop the accumulator is read with tcgen05.ld into a shared-memory partial
-// tile and handed to the same split-K (cluster / distributed shared memory) reduction and
-// fused epilogues as the mma.sync kernel (qgemm.cuh). TMA loads never use multicast.
+// D[128 weight rows, NTILE tokens] (fp32, TMEM) += A[128, 16] . B[NTILE, 16]^T per MMA, with
+// four warp roles per CTA:
+//  * a weight producer (one thread) streams packed 128-row x 64-k tiles and their scales by
+//    TMA into a ring of up to 12 stages, starting before griddepcontrol.wait;
+//  * an activation producer (one thread) streams the [NTILE, 64] fp16 activation tiles
+//    (TMA, SWIZZLE_128B; rows past M and k past K read as zero) into a shorter ring;
+//  * eight dequantisation warps turn each packed tile into fp16 (q - 8) * scale with the
+//    magic-exponent trick and store it as a 128B-swizzled K-major tile (the canonical UMMA
+//    layout) into a small ring, releasing the packed slot as soon as it is in registers;
+//  * one thread issues tcgen05.mma.kind::f16; tcgen05.commit releases the activation and
+//    A slots. Each handshake is one elected arrival per warp.
+// Decode tiles (NTILE <= 64) use ~106 KB of shared memory so two CTAs share an SM.
+// After the K loop the accumulator is read with tcgen05.ld and handed to the same split-K
+// (cluster / distributed shared memory) reduction and fused epilogues as the mma.sync
+// kernel (qgemm.cuh). TMA loads never use multicast.
 //
 // Every mbarrier wait is bounded (~2 s of globaltimer); on expiry the CTA records
 // ORCH device check bit 8, stops issuing, drains what it issued and frees its TMEM.
@@ -28,10 +32,8 @@
 
 namespace orch {
 
-constexpr int kTcThreads = 128;
 constexpr int kTcRows = 128;
 constexpr int kTcBK = 64;  // k per stage: one 128-byte swizzle row of fp16
-constexpr int kTcStages = 4;
 constexpr int kTcABytes = kTcRows * kTcBK * 2;  // 16 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
@@ -75,6 +77,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
           smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -140,6 +149,21 @@ __device__ __forceinline__ uint4 dq8_natural(uint32_t w, uint32_t sc) {
   return o;
 }
 
+// Eight nibbles of the tiled layout (stored k0 k2 k4 k6 k1 k3 k5 k7) -> eight fp16
+// (q - 8) * scale in natural k order, with no byte permutes.
+__device__ __forceinline__ uint4 dq8_tiled(uint32_t w, uint32_t sc) {
+  const __half2 s2 = bits_h2(sc);
+  const __half2 magic_sub = bits_h2(0x64086408u);
+  const __half2 hi_mul = bits_h2(0x2C002C00u), hi_add = bits_h2(0xD480D480u);
+  const uint32_t v = w >> 8;
+  uint4 o;
+  o.x = h2_bits(__hmul2(__hsub2(bits_h2(lop3_and_or(w, 0x000F000Fu, 0x64006400u)), magic_sub), s2));
+  o.y = h2_bits(__hmul2(__hfma2(bits_h2(lop3_and_or(w, 0x00F000F0u, 0x64006400u)), hi_mul, hi_add), s2));
+  o.z = h2_bits(__hmul2(__hsub2(bits_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u)), magic_sub), s2));
+  o.w = h2_bits(__hmul2(__hfma2(bits_h2(lop3_and_or(v, 0x00F000F0u, 0x64006400u)), hi_mul, hi_add), s2));
+  return o;
+}
+
 // Bounded wait that also gives up as soon as another role of the CTA has failed.
 __device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, volatile int* failed) {
   if (mbar_try(bar, parity)) return true;
@@ -155,28 +179,43 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 
 constexpr int kWBytes = kTcRows * (kTcBK / 2);  // packed INT4 tile: 128 rows x 32 bytes
 constexpr int kSBytes = kTcRows * 16;           // scales for 4 stages: 128 rows x 8 fp16
-constexpr int kARing = 2;
 constexpr int kSRing = 4;
 constexpr int kWarpsDq = 8;                       // dequantisation warps (0-3 also run the epilogue)
-constexpr int kWarpProd = kWarpsDq;               // TMA producer warp
-constexpr int kWarpMma = kWarpsDq + 1;            // MMA issuer warp
-constexpr int kTcThreads2 = (kWarpsDq + 2) * 32;
+constexpr int kWarpProdW = kWarpsDq;              // TMA producer of weights and scales
+constexpr int kWarpProdX = kWarpsDq + 1;          // TMA producer of activations
+constexpr int kWarpMma = kWarpsDq + 2;            // MMA issuer
+constexpr int kTcThreads2 = (kWarpsDq + 3) * 32;
 
+// Shared-memory plan. Weights (from HBM) and activations (from L2) have separate rings so
+// the weight stream can run far ahead without holding activation tiles: a weight slot is
+// released by the dequantisation warps, an activation slot by the MMA's commit.
+// Decode tiles (NTILE <= 64) fit two CTAs per SM; prefill tiles take the whole SM.
 template <int NTILE>
 struct TcCfg {
-  static constexpr int S = NTILE <= 32 ? 8 : (NTILE <= 64 ? 6 : 4);  // TMA ring stages
-  static constexpr int AHEAD = S - 2;                                 // stages in flight
+  static constexpr bool kDecode = NTILE <= 64;
+  static constexpr int SW = NTILE <= 16 ? 12 : (NTILE <= 32 ? 10 : 8);  // weight ring (<= 12, see below)
+  static constexpr int SX = NTILE <= 16 ? 8 : (NTILE <= 32 ? 6 : (NTILE <= 64 ? 4 : 3));
+  static constexpr int AR = kDecode ? 2 : 4;  // dequantised-A ring
   static constexpr int XBytes = NTILE * kTcBK * 2;
   static constexpr int OffA = 0;
-  static constexpr int OffX = OffA + kARing * kTcABytes;
-  static constexpr int OffW = OffX + S * XBytes;
-  static constexpr int OffS = OffW + S * kWBytes;
+  static constexpr int OffX = OffA + AR * kTcABytes;
+  static constexpr int OffW = OffX + SX * XBytes;
+  static constexpr int OffS = OffW + SW * kWBytes;
   static constexpr int OffBar = OffS + kSRing * kSBytes;
-  static constexpr int Bytes = OffBar + 256;
+  static constexpr int Bytes = OffBar + 512;
+  static constexpr int kMinBlocks = kDecode ? 2 : 1;
+  // A scale slot is refilled 16 stages after its first use; the weight producer only runs
+  // SW stages ahead of the dequantisation warps, so SW <= 12 keeps every slot live.
+  static_assert(SW <= 12, "scale ring reuse");
+  static_assert(2 * SW + 2 * SX + 2 * AR + 1 <= 62, "barrier area");
+  // the split-K receive buffer reuses the rings and must stay below the barriers
+  static_assert((kTcRows + 16) * NTILE * 4 <= OffBar, "receive buffer");
 };
 
-template <int EPI, int NTILE>
-__global__ void __launch_bounds__(kTcThreads2, 1)
+// LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 32 bytes.
+// LAY 1: weights in the tiled layout (qgemm.cuh), read by contiguous bulk copies.
+template <int EPI, int NTILE, int LAY>
+__global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                     const __grid_constant__ CUtensorMap tms, const QArgs a0) {
   using C = TcCfg<NTILE>;
@@ -189,11 +228,13 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   uint8_t* sX = sm + C::OffX;
   uint8_t* sW = sm + C::OffW;
   uint8_t* sS = sm + C::OffS;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OffBar);
-  uint64_t* empty = full + C::S;
-  uint64_t* afull = empty + C::S;
-  uint64_t* aempty = afull + kARing;
-  uint64_t* done = aempty + kARing;
+  uint64_t* fullW = reinterpret_cast<uint64_t*>(sm + C::OffBar);
+  uint64_t* emptyW = fullW + C::SW;
+  uint64_t* fullX = emptyW + C::SW;
+  uint64_t* emptyX = fullX + C::SX;
+  uint64_t* afull = emptyX + C::SX;
+  uint64_t* aempty = afull + C::AR;
+  uint64_t* done = aempty + C::AR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -202,20 +243,24 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   const int R0 = blockIdx.x * kTcRows;
   const int tok0 = blockIdx.z * NTILE;
   // K is split over the cluster in blocks of 4 stages (one scale tile per block)
-  const int nst_total = (a0.K + kTcBK - 1) / kTcBK;
-  const int nblk = (nst_total + 3) / 4;
+  const int nblk = (a0.K + 4 * kTcBK - 1) / (4 * kTcBK);
+  const int nst_total = LAY == 1 ? 4 * nblk : (a0.K + kTcBK - 1) / kTcBK;
   const int st0 = ((ks * nblk) / KS) * 4;
   const int st1 = min(nst_total, (((ks + 1) * nblk) / KS) * 4);
   const int nst = st1 - st0;
 
   if (warp == 0) tmem_alloc(tmem_slot, kCols);
   if (tid == 0) {
-    for (int i = 0; i < C::S; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+    for (int i = 0; i < C::SW; ++i) {
+      mbar_init(&fullW[i], 1);
+      mbar_init(&emptyW[i], kWarpsDq);  // one elected lane per dequantisation warp
     }
-    for (int i = 0; i < kARing; ++i) {
-      mbar_init(&afull[i], kWarpsDq * 32);  // every dequantisation thread arrives
+    for (int i = 0; i < C::SX; ++i) {
+      mbar_init(&fullX[i], 1);
+      mbar_init(&emptyX[i], 1);
+    }
+    for (int i = 0; i < C::AR; ++i) {
+      mbar_init(&afull[i], kWarpsDq);
       mbar_init(&aempty[i], 1);
     }
     mbar_init(done, 1);
@@ -230,48 +275,66 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   const uint32_t tmem_d = *tmem_slot;
 
   bool done_ok = true;
-  if (warp == kWarpProd) {
-    // ---------------- TMA producer: one thread, runs up to S - 2 stages ahead ----------------
+  if (warp == kWarpProdW) {
+    // ------------- weight producer: packed tiles + scales, up to SW stages ahead -------------
+    // Weights are written only by the packers, which release dependents on exit, so this
+    // stream starts before griddepcontrol.wait and overlaps the previous kernel's tail.
     if (lane == 0) {
       int issued = 0;
-      auto load_wx = [&](int p, bool with_x) {
-        const int v = p % C::S;
-        const bool with_s = (p & 3) == 0;
-        const int k0 = (st0 + p) * kTcBK;
-        mbar_expect_tx(&full[v], (uint32_t)(kWBytes + C::XBytes + (with_s ? kSBytes : 0)));
-        tma_load_2d(sW + v * kWBytes, &tmw, &full[v], k0 >> 1, R0);
-        if (with_s) tma_load_2d(sS + ((p >> 2) % kSRing) * kSBytes, &tms, &full[v], k0 >> 5, R0);
-        if (with_x) tma_load_2d(sX + v * C::XBytes, &tmx, &full[v], k0, tok0);
-      };
-      // weights and scales do not depend on the previous kernel: start streaming them first
-      const int pre = min(C::AHEAD, nst);
-      for (int p = 0; p < pre; ++p) load_wx(p, false);
-      pdl_wait();  // activations may come from the previous kernel
-      for (int p = 0; p < pre; ++p) tma_load_2d(sX + p * C::XBytes, &tmx, &full[p], (st0 + p) * kTcBK, tok0);
-      issued = pre;
-      for (int p = pre; p < nst && !*failed; ++p) {
-        const int v = p % C::S;
-        if (p >= C::S && !mbar_wait_f(&empty[v], (uint32_t)(p / C::S - 1) & 1, failed)) {
+      for (int p = 0; p < nst && !*failed; ++p) {
+        const int v = p % C::SW;
+        if (p >= C::SW && !mbar_wait_f(&emptyW[v], (uint32_t)(p / C::SW - 1) & 1, failed)) {
           *failed = 1;
           break;
         }
-        load_wx(p, true);
+        const bool with_s = (p & 3) == 0;
+        mbar_expect_tx(&fullW[v], (uint32_t)(kWBytes + (with_s ? kSBytes : 0)));
+        if (LAY == 1) {
+          const uint8_t* blk = a0.w + ((size_t)blockIdx.x * nblk + ((st0 + p) >> 2)) * kQ4tBlockBytes;
+          bulk_load(sW + v * kWBytes, blk + ((st0 + p) & 3) * kQ4tStageBytes, kWBytes, &fullW[v]);
+          if (with_s) bulk_load(sS + ((p >> 2) % kSRing) * kSBytes, blk + 4 * kQ4tStageBytes, kSBytes, &fullW[v]);
+        } else {
+          const int k0 = (st0 + p) * kTcBK;
+          tma_load_2d(sW + v * kWBytes, &tmw, &fullW[v], k0 >> 1, R0);
+          if (with_s) tma_load_2d(sS + ((p >> 2) % kSRing) * kSBytes, &tms, &fullW[v], k0 >> 5, R0);
+        }
         issued = p + 1;
       }
       // loads still in flight when the consumers gave up: wait for them before exiting
       if (*failed)
-        for (int p = max(0, issued - C::S); p < issued; ++p) mbar_wait(&full[p % C::S], (uint32_t)(p / C::S) & 1);
-    } else {
-      pdl_wait();
+        for (int p = max(0, issued - C::SW); p < issued; ++p) mbar_wait(&fullW[p % C::SW], (uint32_t)(p / C::SW) & 1);
     }
+    // The other lanes wait here, inactive: spinning on an mbarrier beside the issuing lane
+    // would take its issue slots (and a blocked try_wait stalls the whole warp).
+    __syncwarp();
+    pdl_wait();
+  } else if (warp == kWarpProdX) {
+    // ------------- activation producer: up to SX stages ahead of the MMA -------------
+    pdl_wait();  // activations may come from the previous kernel
+    if (lane == 0) {
+      int issued = 0;
+      for (int p = 0; p < nst && !*failed; ++p) {
+        const int v = p % C::SX;
+        if (p >= C::SX && !mbar_wait_f(&emptyX[v], (uint32_t)(p / C::SX - 1) & 1, failed)) {
+          *failed = 1;
+          break;
+        }
+        mbar_expect_tx(&fullX[v], (uint32_t)C::XBytes);
+        tma_load_2d(sX + v * C::XBytes, &tmx, &fullX[v], (st0 + p) * kTcBK, tok0);
+        issued = p + 1;
+      }
+      if (*failed)
+        for (int p = max(0, issued - C::SX); p < issued; ++p) mbar_wait(&fullX[p % C::SX], (uint32_t)(p / C::SX) & 1);
+    }
+    __syncwarp();
   } else if (warp == kWarpMma) {
     // ---------------- MMA issuer: one thread ----------------
     pdl_wait();
     if (lane == 0) {
       for (int s = 0; s < nst && !*failed; ++s) {
-        const int v = s % C::S, ai = s % kARing;
-        if (!mbar_wait_f(&full[v], (uint32_t)(s / C::S) & 1, failed) ||
-            !mbar_wait_f(&afull[ai], (uint32_t)(s / kARing) & 1, failed)) {
+        const int v = s % C::SX, ai = s % C::AR;
+        if (!mbar_wait_f(&fullX[v], (uint32_t)(s / C::SX) & 1, failed) ||
+            !mbar_wait_f(&afull[ai], (uint32_t)(s / C::AR) & 1, failed)) {
           *failed = 1;
           break;
         }
@@ -281,39 +344,63 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 #pragma unroll
         for (int kk = 0; kk < kTcBK / 16; ++kk)
           umma_f16(tmem_d, ad + 2 * kk, bd + 2 * kk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&empty[v]);
+        umma_commit(&emptyX[v]);
         umma_commit(&aempty[ai]);
       }
       umma_commit(done);
     }
+    __syncwarp();
   } else {
     // ---------------- dequantisation warps: packed tile -> swizzled fp16 A tile ----------------
     pdl_wait();
     const int rs = lane >> 3, c = lane & 7;
     for (int s = 0; s < nst; ++s) {
-      const int v = s % C::S, ai = s % kARing;
-      if (!mbar_wait_f(&full[v], (uint32_t)(s / C::S) & 1, failed)) {
-        *failed = 1;
-        break;
-      }
-      if (s >= kARing && !mbar_wait_f(&aempty[ai], (uint32_t)(s / kARing - 1) & 1, failed)) {
+      const int v = s % C::SW, ai = s % C::AR;
+      bool ok = mbar_wait_f(&fullW[v], (uint32_t)(s / C::SW) & 1, failed);
+      if (ok && s >= C::AR) ok = mbar_wait_f(&aempty[ai], (uint32_t)(s / C::AR - 1) & 1, failed);
+      if (!__all_sync(0xffffffffu, ok)) {  // the warp leaves together (it synchronises below)
         *failed = 1;
         break;
       }
       const uint8_t* wt = sW + v * kWBytes;
       const __half* st = reinterpret_cast<const __half*>(sS + ((s >> 2) % kSRing) * kSBytes);
       uint8_t* at = sA + ai * kTcABytes;
+      if (LAY == 1) {
+        // warps 0-3: k 0..31 of the stage, warps 4-7: k 32..63; one row per thread
+        const int h = warp >> 2, r = (warp & 3) * 32 + lane;
+        const uint4 w4 = *reinterpret_cast<const uint4*>(wt + h * (kWBytes / 2) + r * 16);
+        const uint32_t sc = h2_bits(__half2half2(st[((s & 3) * 2 + h) * kTcRows + r]));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
+        uint8_t* arow = at + (r >> 3) * 1024 + (r & 7) * 128;
+        const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(arow + (((h * 4 + i) ^ (r & 7)) << 4)) = dq8_tiled(wv[i], sc);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[ai]);
+        continue;
+      }
       const int sj = (s & 3) * 2 + (c >> 2);
+      uint32_t w[kTcRows / (4 * kWarpsDq)], sc[kTcRows / (4 * kWarpsDq)];
 #pragma unroll
       for (int i = 0; i < kTcRows / (4 * kWarpsDq); ++i) {
         const int r = warp * (kTcRows / kWarpsDq) + 4 * i + rs;
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(wt + r * 32 + c * 4);
-        const uint32_t sc = h2_bits(__half2half2(st[r * 8 + sj]));
-        *reinterpret_cast<uint4*>(at + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
-            dq8_natural(w, sc);
+        w[i] = *reinterpret_cast<const uint32_t*>(wt + r * 32 + c * 4);
+        sc[i] = h2_bits(__half2half2(st[r * 8 + sj]));
       }
-      fence_proxy_async();
-      mbar_arrive(&afull[ai]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
+#pragma unroll
+      for (int i = 0; i < kTcRows / (4 * kWarpsDq); ++i) {
+        const int r = warp * (kTcRows / kWarpsDq) + 4 * i + rs;
+        *reinterpret_cast<uint4*>(at + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
+            dq8_natural(w[i], sc[i]);
+      }
+      fence_proxy_async();  // make this thread's generic-proxy stores visible to the MMA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[ai]);
     }
   }
   done_ok = mbar_wait(done, 0);
@@ -332,13 +419,10 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       uint32_t r[16];
       tmem_ld16(tmem_d + ((uint32_t)(32 * warp) << 16) + (uint32_t)cc, r);
       float* dst = epi_dest<EPI, kTcRows>(cl, recv, Mp, KS, ks, tid, cc);
+      const int pitch = epi_pitch<EPI, kTcRows>(KS);
 #pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        if (cc + j < Mp)
-          *reinterpret_cast<float4*>(dst + j) =
-              bad ? make_float4(0.f, 0.f, 0.f, 0.f)
-                  : make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                __uint_as_float(r[j + 3]));
+      for (int j = 0; j < 16; ++j)
+        if (cc + j < Mp) dst[j * pitch] = bad ? 0.f : __uint_as_float(r[j]);
     }
   }
   tc_fence_before();
@@ -404,12 +488,12 @@ size_t tc_smem_bytes(int ntile) {
   }
 }
 
-template <int EPI, int NTILE>
+template <int EPI, int NTILE, int LAY>
 int tc_launch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int KS,
               cudaStream_t st) {
   static bool attr_done[64] = {};
   const int dev = device_index();
-  auto kern = tc_qgemm_kernel<EPI, NTILE>;
+  auto kern = tc_qgemm_kernel<EPI, NTILE, LAY>;
   const size_t smem = tc_smem_bytes(NTILE);
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     ORCH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -430,37 +514,47 @@ static uint32_t g_tc_min_m = [] {
 uint32_t tc_min_m() { return g_tc_min_m; }
 void set_tc_min_m(uint32_t m) { g_tc_min_m = m; }
 
+template <int EPI, int LAY>
+int tc_dispatch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int ntile,
+                int KS, cudaStream_t st) {
+  switch (ntile) {
+    case 16: return tc_launch<EPI, 16, LAY>(mx, mw, ms, a, KS, st);
+    case 32: return tc_launch<EPI, 32, LAY>(mx, mw, ms, a, KS, st);
+    case 64: return tc_launch<EPI, 64, LAY>(mx, mw, ms, a, KS, st);
+    case 128: return tc_launch<EPI, 128, LAY>(mx, mw, ms, a, KS, st);
+    default: return tc_launch<EPI, 256, LAY>(mx, mw, ms, a, KS, st);
+  }
+}
+
 template <int EPI>
 int tc_qgemm_run(QArgs a, cudaStream_t st) {
-  // tensor maps need 16-byte row strides: K % 256 == 0 for the scale rows
-  if (a.x_f32 || a.M < 1 || (a.K % 256) != 0 || !encode_fn()) return ORCH_ERR_UNSUPPORTED;
-  if (((uintptr_t)a.x & 15) != 0 || ((uintptr_t)a.w & 15) != 0 || ((uintptr_t)a.s & 15) != 0)
+  // Reference layout: tensor maps need 16-byte row strides, so K % 256 == 0 for the scale
+  // rows. Tiled layout: any K % 32 == 0 (the layout is padded to 256).
+  const bool tiled = a.tiled != 0;
+  if (a.x_f32 || a.M < 1 || (!tiled && (a.K % 256) != 0) || (a.K % 8) != 0 || !encode_fn())
+    return ORCH_ERR_UNSUPPORTED;
+  if (((uintptr_t)a.x & 15) != 0 || ((uintptr_t)a.w & 15) != 0 || (!tiled && ((uintptr_t)a.s & 15) != 0))
     return ORCH_ERR_UNSUPPORTED;
   a.check = device_check_word();
   const int ntile = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
   CUtensorMap mx, mw, ms;
-  const bool ok = encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
-                           (uint64_t)a.K * 2, kTcBK, ntile, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                  encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
-                           (uint64_t)(a.K / 2), kTcBK / 2, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-                  encode2d(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.s, (uint64_t)(a.K / 32), (uint64_t)a.N,
-                           (uint64_t)(a.K / 32) * 2, 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  bool ok = encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,
+                     kTcBK, ntile, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (ok && !tiled)
+    ok = encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N, (uint64_t)(a.K / 2),
+                  kTcBK / 2, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         encode2d(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.s, (uint64_t)(a.K / 32), (uint64_t)a.N,
+                  (uint64_t)(a.K / 32) * 2, 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!ok) return fail(ORCH_ERR_UNSUPPORTED, "tensor map encode failed");
-  const int nblk = (a.K / kTcBK + 3) / 4;
+  if (tiled) mw = ms = mx;  // unused by the tiled kernel
+  const int nblk = (a.K + 4 * kTcBK - 1) / (4 * kTcBK);
   const int tiles = ((a.N + kTcRows - 1) / kTcRows) * ((a.M + ntile - 1) / ntile);
-  const int per_sm = tc_smem_bytes(ntile) * 2 <= 227 * 1024 ? 2 : 1;
+  const int per_sm = ntile <= 64 ? 2 : 1;  // TcCfg::kMinBlocks
   // split K only as far as one wave of CTAs covers the SMs
   const int slots = per_sm * num_sms();
   int KS = 1;
   while (KS < 8 && tiles * KS * 2 <= slots && nblk >= KS * 4) KS *= 2;
-  int rc;
-  switch (ntile) {
-    case 16: rc = tc_launch<EPI, 16>(mx, mw, ms, a, KS, st); break;
-    case 32: rc = tc_launch<EPI, 32>(mx, mw, ms, a, KS, st); break;
-    case 64: rc = tc_launch<EPI, 64>(mx, mw, ms, a, KS, st); break;
-    case 128: rc = tc_launch<EPI, 128>(mx, mw, ms, a, KS, st); break;
-    default: rc = tc_launch<EPI, 256>(mx, mw, ms, a, KS, st); break;
-  }
+  const int rc = tiled ? tc_dispatch<EPI, 1>(mx, mw, ms, a, ntile, KS, st) : tc_dispatch<EPI, 0>(mx, mw, ms, a, ntile, KS, st);
   if (rc != ORCH_OK) return rc;
   return check_launch("tc_qgemm");
 }

@@ -1,6 +1,8 @@
 """Kernel-level timing of the decode path's kernels at the 7B shapes.
 
-    python -m orchard_b200.kbench [--kernel q4|q8pc|attn|all] [--M 1,16,64] [--reps 50]
+    python -m orchard_b200.kbench [--kernel q4|q4t|q8pc|attn|all] [--M 1,16,64] [--reps 50]
+
+q4: reference-layout INT4 weights (orch_gemm_q4_0_ex); q4t: tiled INT4 weights (orch_q4t_gemm).
 
 Each INT4/INT8 GEMM shape is timed over enough distinct weight copies that the set
 exceeds the 126 MB L2 (so every launch streams its weights from HBM), with CUDA events on
@@ -51,14 +53,18 @@ def _copies(nbytes: int) -> int:
 
 def time_q4(M: int, K: int, N: int, reps: int, fmt: str = "q4"):
     dev = "cuda"
-    wbytes = N * K // 2 if fmt == "q4" else N * K
-    sbytes = N * K // 16 if fmt == "q4" else 2 * N
+    wbytes = N * K // 2 if fmt in ("q4", "q4t") else N * K
+    sbytes = N * K // 16 if fmt in ("q4", "q4t") else 2 * N
     n = min(_copies(wbytes + sbytes), 64)
     ws = []
     for i in range(n):
-        if fmt == "q4":
+        if fmt in ("q4", "q4t"):
             w = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev)
             s = (torch.rand((N, K // 32), device=dev) * 0.01).half()
+            if fmt == "q4t":
+                t = torch.empty(_lib.lib().orch_q4t_bytes(N, K), dtype=torch.uint8, device=dev)
+                call("orch_q4t_pack", w, s, N, K, t, torch.cuda.current_stream().cuda_stream)
+                w, s = t, None
         else:
             w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev)
             s = (torch.rand(N, device=dev) * 0.01).half()
@@ -69,7 +75,10 @@ def time_q4(M: int, K: int, N: int, reps: int, fmt: str = "q4"):
 
     def run(i):
         w, s = ws[i % n]
-        call(fn, w, s, x, F16, y, F32, K, N, M, torch.cuda.current_stream().cuda_stream)
+        if fmt == "q4t":
+            call("orch_q4t_gemm", w, x, y, F32, K, N, M, torch.cuda.current_stream().cuda_stream)
+        else:
+            call(fn, w, s, x, F16, y, F32, K, N, M, torch.cuda.current_stream().cuda_stream)
 
     us = _graph_time(run, n, reps)
     byts = wbytes + sbytes + 2 * M * K + 4 * M * N
@@ -100,7 +109,7 @@ def time_attn(M: int, L: int, reps: int, nh: int = 32, hd: int = 128, max_seq: i
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default="all", choices=["q4", "q8pc", "attn", "all"])
+    ap.add_argument("--kernel", default="all", choices=["q4", "q4t", "q8pc", "attn", "all"])
     ap.add_argument("--M", default="1,16,64")
     ap.add_argument("--shape", default="", help="only this decode shape name (qkv, o, gate_up, down, lm_head)")
     ap.add_argument("--reps", type=int, default=50)
@@ -108,11 +117,11 @@ def main():
     call("orch_init", 0, None)
     Ms = [int(v) for v in a.M.split(",")]
     for M in Ms:
-        if a.kernel in ("q4", "q8pc", "all"):
+        if a.kernel in ("q4", "q4t", "q8pc", "all"):
             for name, K, N in DECODE_SHAPES:
                 if a.shape and name != a.shape:
                     continue
-                for fmt in (("q4", "q8pc") if a.kernel == "all" else (a.kernel,)):
+                for fmt in (("q4t", "q4", "q8pc") if a.kernel == "all" else (a.kernel,)):
                     r = time_q4(M, K, N, a.reps, fmt)
                     r["shape"] = name
                     print(json.dumps(r), flush=True)

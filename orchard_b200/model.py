@@ -128,8 +128,22 @@ def interleave_gate_up(p1, s1, p3, s3):
     return il(p1, p3).contiguous(), il(s1, s3).contiguous()
 
 
+def tile_q4(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """Re-lays a packed INT4 weight (reference layout, on the device) into the tiled layout
+    the tensor-core GEMM streams (rows in tiles of 128, k in blocks of 256, each block one
+    contiguous run of nibbles and scales; see include/orchard_b200.h)."""
+    N, K = w.shape[0], w.shape[1] * 2
+    t = torch.empty(_lib.lib().orch_q4t_bytes(N, K), dtype=torch.uint8, device=w.device)
+    call("orch_q4t_pack", ptr(w), ptr(s), N, K, ptr(t), _stream())
+    return t
+
+
 class DeviceLayer:
-    def __init__(self, entries: dict, cfg: LlamaConfig, device):
+    """One layer's device weights: fused [Wq;Wk;Wv], Wo, gate/up interleaved, Wdown, either in
+    the tiled layout (`tiled`, the default: tcgen05 GEMM for every row count) or in the
+    reference layout (mma.sync GEMV below the tensor-core threshold)."""
+
+    def __init__(self, entries: dict, cfg: LlamaConfig, device, tiled: bool = True):
         H, F = cfg.hidden_size, cfg.intermediate_size
         q = {n: _packed_on_device(entries[n], device) for n in ("wq", "wk", "wv", "wo", "w1", "w3", "w2")}
         self.wqkv = torch.cat([q["wq"][0], q["wk"][0], q["wv"][0]]).contiguous()
@@ -137,15 +151,25 @@ class DeviceLayer:
         self.wo, self.so = q["wo"]
         self.w13, self.s13 = interleave_gate_up(q["w1"][0], q["w1"][1], q["w3"][0], q["w3"][1])
         self.w2, self.s2 = q["w2"]
+        del q
         self.attn_norm = torch.as_tensor(np.asarray(entries["attn_norm"], np.float32)).to(device)
         self.ffn_norm = torch.as_tensor(np.asarray(entries["ffn_norm"], np.float32)).to(device)
         assert self.wqkv.shape == (3 * H, H // 2) and self.w13.shape == (2 * F, H // 2)
         assert self.w2.shape == (H, F // 2)
+        self.tiled = tiled
+        if tiled:
+            self.tqkv = tile_q4(self.wqkv, self.sqkv)
+            self.to = tile_q4(self.wo, self.so)
+            self.t13 = tile_q4(self.w13, self.s13)
+            self.t2 = tile_q4(self.w2, self.s2)
+            torch.cuda.current_stream().synchronize()
+            self.wqkv = self.sqkv = self.wo = self.so = self.w13 = self.s13 = self.w2 = self.s2 = None
         self.lora: Dict[str, tuple] = {}
 
     def weight_bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in
-                   (self.wqkv, self.sqkv, self.wo, self.so, self.w13, self.s13, self.w2, self.s2))
+        ts = (self.tqkv, self.to, self.t13, self.t2) if self.tiled else \
+            (self.wqkv, self.sqkv, self.wo, self.so, self.w13, self.s13, self.w2, self.s2)
+        return sum(t.numel() * t.element_size() for t in ts)
 
     def set_lora(self, mods: Dict[str, tuple], cfg: LlamaConfig, r: int, device):
         """Packs adapters per fused projection: A_cat [K, R*r] and B_cat [R, r, width]."""
@@ -201,7 +225,8 @@ class RowBuffers:
 class DecodeEngine:
     """Device state for up to ``max_batch`` sequences of up to ``max_seq`` positions."""
 
-    def __init__(self, ck: Checkpoint, device=0, max_batch: int = 32, max_seq: Optional[int] = None):
+    def __init__(self, ck: Checkpoint, device=0, max_batch: int = 32, max_seq: Optional[int] = None,
+                 tiled: bool = True):
         if not torch.cuda.is_available():
             raise RuntimeError("orchard_b200 needs a CUDA device (there is no CPU fallback)")
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
@@ -215,13 +240,18 @@ class DecodeEngine:
         self.max_seq = max_seq or cfg.max_position_embeddings
         self.max_pos = max(self.max_seq, cfg.max_position_embeddings)
         dev = self.device
-        self.layers = [DeviceLayer(e, cfg, dev) for e in ck.layers]
+        self.tiled = tiled
+        self.layers = [DeviceLayer(e, cfg, dev, tiled) for e in ck.layers]
         emb = ck.embed if isinstance(ck.embed, torch.Tensor) else torch.as_tensor(np.asarray(ck.embed))
         if emb.dtype not in (torch.float16, torch.float32):
             emb = emb.float()
         self.embed = emb.to(dev).contiguous()
         self.norm = torch.as_tensor(np.asarray(ck.norm, np.float32)).to(dev)
         self.lm_w, self.lm_s = _packed_on_device(ck.lm_head, dev)
+        if tiled:
+            self.lm_t = tile_q4(self.lm_w, self.lm_s)
+            torch.cuda.current_stream().synchronize()
+            self.lm_w = self.lm_s = None
         cos, sin = precompute_freqs_cis(cfg.head_dim, self.max_pos, cfg.rope_theta)
         self.cos = torch.as_tensor(cos).to(dev)
         self.sin = torch.as_tensor(sin).to(dev)
@@ -274,18 +304,32 @@ class DecodeEngine:
             kc, vc = self.k_cache[li], self.v_cache[li]
             call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.attn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
             lt, lb, lr = self._lora(L, "qkv", b.xn, M, s, b)
-            call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
-                 ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
-                 self.max_seq, lt, lb, lr, s)
+            if L.tiled:
+                call("orch_q4t_qkv_rope", ptr(L.tqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos), ptr(b.slots),
+                     ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc), self.max_seq,
+                     lt, lb, lr, s)
+            else:
+                call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
+                     ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
+                     self.max_seq, lt, lb, lr, s)
             call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
                  ptr(b.attn), M, nh, hd, self.max_seq, ptr(b.attn_ws), b.attn_ws_bytes, s)
             lt, lb, lr = self._lora(L, "o", b.attn, M, s, b)
-            call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
+            if L.tiled:
+                call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
+            else:
+                call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
             call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.ffn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
             lt, lb, lr = self._lora(L, "gu", b.xn, M, s, b)
-            call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
+            if L.tiled:
+                call("orch_q4t_linear_swiglu", ptr(L.t13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
+            else:
+                call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
             lt, lb, lr = self._lora(L, "down", b.h, M, s, b)
-            call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
+            if L.tiled:
+                call("orch_q4t_linear_resid", ptr(L.t2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
+            else:
+                call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
 
     def run_head(self, M: int):
         """Final RMSNorm, INT4 lm_head (fp32 logits) and argmax into tok_out."""
@@ -293,8 +337,11 @@ class DecodeEngine:
         cfg, s = self.cfg, _stream()
         H, V = cfg.hidden_size, cfg.vocab_size
         call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(self.norm), F32, ptr(b.xn), F16, cfg.rms_norm_eps, H, M, s)
-        call("orch_gemm_q4_0_ex", ptr(self.lm_w), ptr(self.lm_s), ptr(b.xn), F16, ptr(b.logits), F32,
-             H, V, M, s)
+        if self.tiled:
+            call("orch_q4t_gemm", ptr(self.lm_t), ptr(b.xn), ptr(b.logits), F32, H, V, M, s)
+        else:
+            call("orch_gemm_q4_0_ex", ptr(self.lm_w), ptr(self.lm_s), ptr(b.xn), F16, ptr(b.logits), F32,
+                 H, V, M, s)
         call("orch_argmax_rows", ptr(b.logits), M, V, ptr(b.tok_out), s)
 
     def prefill_rows(self, tokens: np.ndarray, positions: np.ndarray, slots: np.ndarray, chunk: int = 4096):
@@ -371,10 +418,10 @@ class Llama:
 
     def __init__(self, model_path: Optional[str] = None, *, checkpoint: Optional[Checkpoint] = None,
                  device=0, max_batch: int = 32, max_seq: Optional[int] = None, tokenizer=None,
-                 use_graphs: bool = True):
+                 use_graphs: bool = True, tiled: bool = True):
         ck = checkpoint if checkpoint is not None else load_checkpoint(model_path)
         self.config = dict(ck.config)
-        self.engine = DecodeEngine(ck, device=device, max_batch=max_batch, max_seq=max_seq)
+        self.engine = DecodeEngine(ck, device=device, max_batch=max_batch, max_seq=max_seq, tiled=tiled)
         self.use_graphs = use_graphs
         self.tokenizer = tokenizer
         if tokenizer is None and model_path is not None:

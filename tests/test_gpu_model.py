@@ -2,7 +2,8 @@
 
 * Greedy ``generate_batch`` on the tiny checkpoint reproduces the tokens and logits the
   reference's own ``orchard/model.py`` produced (fixtures in tests/golden/), with and
-  without LoRA. Logit tolerance: max|gpu - ref| / max|ref| <= 1e-2.
+  without LoRA, with the engine's weights in the tiled layout (default) and in the
+  reference layout. Logit tolerance: max|gpu - ref| / max|ref| <= 1e-2.
 * A 2-layer slice of the 7B shape (hidden 4096, 32 heads, FFN 11008, vocab 32000)
   matches the oracle step by step within the same tolerance.
 """
@@ -39,10 +40,11 @@ def run_logits(llm: Llama, prompts, steps):
     return np.stack(toks, 1), lgs
 
 
+@pytest.mark.parametrize("tiled", [True, False])
 @pytest.mark.parametrize("graphs", [True, False])
-def test_generate_matches_reference_golden(golden_model, graphs):
+def test_generate_matches_reference_golden(golden_model, graphs, tiled):
     g = golden_model
-    llm = Llama.from_tensors(g["config"], g["ckpt"], max_batch=4, use_graphs=graphs)
+    llm = Llama.from_tensors(g["config"], g["ckpt"], max_batch=4, use_graphs=graphs, tiled=tiled)
     toks = llm.generate_batch_ids(g["prompts"], max_tokens=g["max_tokens"], temperature=0)
     assert toks == g["tokens"]
     _, lgs = run_logits(llm, g["prompts"], g["max_tokens"])
