@@ -188,7 +188,10 @@ template <int HD>
 static int attn_launch(AttnArgs a, cudaStream_t st) {
   dim3 grid(a.M * a.nh, a.S);
   const dim3 none(0, 0, 0);
-  ORCH_CUDA(launch_k(attn_decode_kernel<HD>, grid, dim3(kAttnThreads), 0, st, none, a));
+  // Not a programmatic dependent: launched early (the QKV GEMM releases dependents at its
+  // start), its many small CTAs occupy the SMs while the GEMM still runs; measured at batch
+  // 64 (7B shape) that made the decode step 12.1 ms instead of 8.1 ms.
+  ORCH_CUDA(launch_k_serial(attn_decode_kernel<HD>, grid, dim3(kAttnThreads), 0, st, none, a));
   if (a.S > 1) ORCH_CUDA(launch_k(attn_combine_kernel<HD>, dim3(a.M * a.nh), dim3(HD), 0, st, none, a));
   return check_launch("attention_decode");
 }

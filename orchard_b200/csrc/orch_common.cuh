@@ -26,10 +26,10 @@ uint32_t* device_check_word();  // per-device flag word, set by kernels' own bou
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 bool pdl_enabled();  // ORCHARD_PDL=0 in the environment turns programmatic launch off
 
-// Launch with programmatic stream serialization (and an optional cluster shape).
+// Launch with an optional cluster shape, and programmatic stream serialization when allowed.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                     dim3 cluster, Args&&... args) {
+cudaError_t launch_k_pdl(bool allow_pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t st, dim3 cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -44,7 +44,7 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
     attr[n].val.clusterDim.z = cluster.z;
     ++n;
   }
-  if (pdl_enabled()) {
+  if (allow_pdl && pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
@@ -52,6 +52,19 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
   cfg.attrs = attr;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// Launch with programmatic dependent launch (when enabled).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster,
+                     Args&&... args) {
+  return launch_k_pdl(true, kern, grid, block, smem, st, cluster, std::forward<Args>(args)...);
+}
+// Launch fully serialised after the previous work in the stream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k_serial(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            dim3 cluster, Args&&... args) {
+  return launch_k_pdl(false, kern, grid, block, smem, st, cluster, std::forward<Args>(args)...);
 }
 
 #define ORCH_REQUIRE(cond, msg)                                  \

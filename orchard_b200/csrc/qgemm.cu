@@ -23,6 +23,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "qgemm.cuh"
 
@@ -293,6 +294,16 @@ int dispatch_nt(const QArgs& a, int KS, size_t smem, cudaStream_t st) {
 
 int rows_per_cta(int M) { return (M > 32) ? 128 : 64; }
 
+// CTAs per SM the cluster K-split aims for (more resident warps keep more weight bytes in
+// flight); ORCHARD_QGEMM_CTAS_PER_SM overrides.
+int ks_target() {
+  static const int v = [] {
+    const char* e = std::getenv("ORCHARD_QGEMM_CTAS_PER_SM");
+    return e ? std::max(1, std::atoi(e)) : 2;
+  }();
+  return v;
+}
+
 }  // namespace
 
 // Splits M into blocks of <= 64 rows that fit shared memory, picks the cluster K-split,
@@ -321,7 +332,7 @@ int qgemm_run(QArgs a, cudaStream_t st) {
     int mb = std::min(64, total_M - m0);
     const int rows = rows_per_cta(mb);
     const int tiles = (a.N + rows - 1) / rows;
-    const int target = 2 * num_sms();
+    const int target = ks_target() * num_sms();
     int KS = 1;
     while (KS < 8 && tiles * KS < target && a.nchunk >= 4 * KS) KS *= 2;
     auto xbytes = [&](int ks, int m) {

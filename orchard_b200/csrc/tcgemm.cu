@@ -7,19 +7,21 @@
 //
 // D[128 weight rows, NTILE tokens] (fp32, TMEM) += A[128, 16] . B[NTILE, 16]^T per MMA, with
 // four warp roles per CTA:
-//  * a weight producer (one thread) streams packed 128-row x 64-k tiles and their scales by
-//    TMA into a ring of up to 12 stages, starting before griddepcontrol.wait;
+//  * a weight producer (one thread) streams packed 128-row x 64-k tiles and their scales
+//    (TMA boxes, or contiguous bulk copies for the tiled layout) into a 12-stage ring,
+//    starting before griddepcontrol.wait;
 //  * an activation producer (one thread) streams the [NTILE, 64] fp16 activation tiles
 //    (TMA, SWIZZLE_128B; rows past M and k past K read as zero) into a shorter ring;
 //  * eight dequantisation warps turn each packed tile into fp16 (q - 8) * scale with the
-//    magic-exponent trick and store it as a 128B-swizzled K-major tile (the canonical UMMA
-//    layout) into a small ring, releasing the packed slot as soon as it is in registers;
-//  * one thread issues tcgen05.mma.kind::f16; tcgen05.commit releases the activation and
-//    A slots. Each handshake is one elected arrival per warp.
-// Decode tiles (NTILE <= 64) use ~106 KB of shared memory so two CTAs share an SM.
-// After the K loop the accumulator is read with tcgen05.ld and handed to the same split-K
-// (cluster / distributed shared memory) reduction and fused epilogues as the mma.sync
-// kernel (qgemm.cuh). TMA loads never use multicast.
+//    magic-exponent trick and store it with tcgen05.st into a ring of A tiles in tensor
+//    memory (6 to 8 stages deep), one weight row per TMEM lane;
+//  * one thread issues tcgen05.mma.kind::f16 with A from tensor memory and B (activations)
+//    from shared memory; tcgen05.commit releases the activation and A slots. Each
+//    handshake is one elected arrival per warp.
+// Decode tiles (NTILE <= 64) use half the tensor memory and ~105 KB of shared memory, so
+// two CTAs share an SM. After the K loop the accumulator is read with tcgen05.ld and handed
+// to the same split-K (cluster / distributed shared memory) reduction and fused epilogues as
+// the mma.sync kernel (qgemm.cuh). TMA loads never use multicast.
 //
 // Every mbarrier wait is bounded (~2 s of globaltimer); on expiry the CTA records
 // ORCH device check bit 8, stops issuing, drains what it issued and frees its TMEM.
@@ -34,7 +36,6 @@ namespace orch {
 
 constexpr int kTcRows = 128;
 constexpr int kTcBK = 64;  // k per stage: one 128-byte swizzle row of fp16
-constexpr int kTcABytes = kTcRows * kTcBK * 2;  // 16 KB
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -97,13 +98,24 @@ __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D (TMEM) += A (TMEM, K-major: row i in lane i, two fp16 of consecutive k per column) . B (smem)
+__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// Sixteen consecutive 32-bit columns of this thread's TMEM lane; waits for completion.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -186,19 +198,23 @@ constexpr int kWarpProdX = kWarpsDq + 1;          // TMA producer of activations
 constexpr int kWarpMma = kWarpsDq + 2;            // MMA issuer
 constexpr int kTcThreads2 = (kWarpsDq + 3) * 32;
 
-// Shared-memory plan. Weights (from HBM) and activations (from L2) have separate rings so
-// the weight stream can run far ahead without holding activation tiles: a weight slot is
-// released by the dequantisation warps, an activation slot by the MMA's commit.
-// Decode tiles (NTILE <= 64) fit two CTAs per SM; prefill tiles take the whole SM.
+// Shared-memory and tensor-memory plan. Weights (from HBM) and activations (from L2) have
+// separate shared-memory rings so the weight stream runs far ahead without holding
+// activation tiles: a weight slot is released by the dequantisation warps, an activation
+// slot by the MMA's commit. The dequantised A tiles live in tensor memory (32 columns per
+// 64-k stage, beside the accumulator), which gives a deep A ring without shared memory.
+// Decode tiles (NTILE <= 64) take half of the SM's tensor memory and ~105 KB of shared
+// memory, so two CTAs share an SM; prefill tiles take the whole SM.
 template <int NTILE>
 struct TcCfg {
   static constexpr bool kDecode = NTILE <= 64;
-  static constexpr int SW = NTILE <= 16 ? 12 : (NTILE <= 32 ? 10 : 8);  // weight ring (<= 12, see below)
-  static constexpr int SX = NTILE <= 16 ? 8 : (NTILE <= 32 ? 6 : (NTILE <= 64 ? 4 : 3));
-  static constexpr int AR = kDecode ? 2 : 4;  // dequantised-A ring
+  static constexpr uint32_t kTmemCols = kDecode ? 256 : 512;
+  static constexpr uint32_t kAccCols = NTILE < 32 ? 32 : NTILE;
+  static constexpr int AR = (kTmemCols - kAccCols) / 32 < 8 ? (int)((kTmemCols - kAccCols) / 32) : 8;
+  static constexpr int SW = 12;  // weight ring (<= 12, see below)
+  static constexpr int SX = NTILE <= 32 ? 8 : (NTILE <= 64 ? 6 : (NTILE <= 128 ? 8 : 5));
   static constexpr int XBytes = NTILE * kTcBK * 2;
-  static constexpr int OffA = 0;
-  static constexpr int OffX = OffA + AR * kTcABytes;
+  static constexpr int OffX = 0;
   static constexpr int OffW = OffX + SX * XBytes;
   static constexpr int OffS = OffW + SW * kWBytes;
   static constexpr int OffBar = OffS + kSRing * kSBytes;
@@ -210,6 +226,7 @@ struct TcCfg {
   static_assert(2 * SW + 2 * SX + 2 * AR + 1 <= 62, "barrier area");
   // the split-K receive buffer reuses the rings and must stay below the barriers
   static_assert((kTcRows + 16) * NTILE * 4 <= OffBar, "receive buffer");
+  static_assert(AR >= 2, "A ring");
 };
 
 // LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 32 bytes.
@@ -220,11 +237,9 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
                     const __grid_constant__ CUtensorMap tms, const QArgs a0) {
   using C = TcCfg<NTILE>;
   extern __shared__ __align__(1024) uint8_t smraw[];
-  constexpr uint32_t kCols = NTILE < 32 ? 32 : NTILE;
   constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NTILE >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = sm + C::OffA;
   uint8_t* sX = sm + C::OffX;
   uint8_t* sW = sm + C::OffW;
   uint8_t* sS = sm + C::OffS;
@@ -249,7 +264,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   const int st1 = min(nst_total, (((ks + 1) * nblk) / KS) * 4);
   const int nst = st1 - st0;
 
-  if (warp == 0) tmem_alloc(tmem_slot, kCols);
+  if (warp == 0) tmem_alloc(tmem_slot, C::kTmemCols);
   if (tid == 0) {
     for (int i = 0; i < C::SW; ++i) {
       mbar_init(&fullW[i], 1);
@@ -273,6 +288,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
+  const uint32_t tmem_a = tmem_d + C::kAccCols;  // A ring: slot i at columns 32 i
 
   bool done_ok = true;
   if (warp == kWarpProdW) {
@@ -328,7 +344,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
-    // ---------------- MMA issuer: one thread ----------------
+    // ---------------- MMA issuer: one thread; A from tensor memory, B from shared ----------------
     pdl_wait();
     if (lane == 0) {
       for (int s = 0; s < nst && !*failed; ++s) {
@@ -339,11 +355,10 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
           break;
         }
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(sA + ai * kTcABytes));
         const uint64_t bd = sw128_desc(smem_u32(sX + v * C::XBytes));
 #pragma unroll
         for (int kk = 0; kk < kTcBK / 16; ++kk)
-          umma_f16(tmem_d, ad + 2 * kk, bd + 2 * kk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ta(tmem_d, tmem_a + ai * 32 + kk * 8, bd + 2 * kk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&emptyX[v]);
         umma_commit(&aempty[ai]);
       }
@@ -351,9 +366,12 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     }
     __syncwarp();
   } else {
-    // ---------------- dequantisation warps: packed tile -> swizzled fp16 A tile ----------------
+    // ------- dequantisation warps: packed tile -> fp16 A tile in tensor memory -------
+    // Warp w owns TMEM lanes 32 (w % 4) .. + 31 (= weight rows); warps 0-3 write k 0..31 of
+    // each stage (columns 0..15 of the slot), warps 4-7 k 32..63 (columns 16..31).
     pdl_wait();
-    const int rs = lane >> 3, c = lane & 7;
+    const int h = warp >> 2, r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     for (int s = 0; s < nst; ++s) {
       const int v = s % C::SW, ai = s % C::AR;
       bool ok = mbar_wait_f(&fullW[v], (uint32_t)(s / C::SW) & 1, failed);
@@ -364,41 +382,29 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
       }
       const uint8_t* wt = sW + v * kWBytes;
       const __half* st = reinterpret_cast<const __half*>(sS + ((s >> 2) % kSRing) * kSBytes);
-      uint8_t* at = sA + ai * kTcABytes;
-      if (LAY == 1) {
-        // warps 0-3: k 0..31 of the stage, warps 4-7: k 32..63; one row per thread
-        const int h = warp >> 2, r = (warp & 3) * 32 + lane;
-        const uint4 w4 = *reinterpret_cast<const uint4*>(wt + h * (kWBytes / 2) + r * 16);
-        const uint32_t sc = h2_bits(__half2half2(st[((s & 3) * 2 + h) * kTcRows + r]));
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
-        uint8_t* arow = at + (r >> 3) * 1024 + (r & 7) * 128;
-        const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          *reinterpret_cast<uint4*>(arow + (((h * 4 + i) ^ (r & 7)) << 4)) = dq8_tiled(wv[i], sc);
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[ai]);
-        continue;
-      }
-      const int sj = (s & 3) * 2 + (c >> 2);
-      uint32_t w[kTcRows / (4 * kWarpsDq)], sc[kTcRows / (4 * kWarpsDq)];
-#pragma unroll
-      for (int i = 0; i < kTcRows / (4 * kWarpsDq); ++i) {
-        const int r = warp * (kTcRows / kWarpsDq) + 4 * i + rs;
-        w[i] = *reinterpret_cast<const uint32_t*>(wt + r * 32 + c * 4);
-        sc[i] = h2_bits(__half2half2(st[r * 8 + sj]));
+      uint4 w4;
+      uint32_t sc;
+      if (LAY == 1) {  // [2 halves][128 rows][16 B], scales [8 groups][128 rows]
+        w4 = *reinterpret_cast<const uint4*>(wt + h * (kWBytes / 2) + r * 16);
+        sc = h2_bits(__half2half2(st[((s & 3) * 2 + h) * kTcRows + r]));
+      } else {  // TMA boxes: [128 rows][32 B], scales [128 rows][8 groups]
+        w4 = *reinterpret_cast<const uint4*>(wt + r * 32 + h * 16);
+        sc = h2_bits(__half2half2(st[r * 8 + (s & 3) * 2 + h]));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
+      const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint32_t q[16];
 #pragma unroll
-      for (int i = 0; i < kTcRows / (4 * kWarpsDq); ++i) {
-        const int r = warp * (kTcRows / kWarpsDq) + 4 * i + rs;
-        *reinterpret_cast<uint4*>(at + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) =
-            dq8_natural(w[i], sc[i]);
+      for (int i = 0; i < 4; ++i) {
+        const uint4 o = LAY == 1 ? dq8_tiled(wv[i], sc) : dq8_natural(wv[i], sc);
+        q[4 * i] = o.x;
+        q[4 * i + 1] = o.y;
+        q[4 * i + 2] = o.z;
+        q[4 * i + 3] = o.w;
       }
-      fence_proxy_async();  // make this thread's generic-proxy stores visible to the MMA
+      tmem_st16(tmem_a + lane_base + ai * 32 + h * 16, q);
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[ai]);
     }
@@ -427,7 +433,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem_d, kCols);
+  if (warp == 0) tmem_dealloc(tmem_d, C::kTmemCols);
   if (tid == 0 && bad) atomicOr(a0.check, 256u);
 
   QArgs a = a0;
