@@ -294,6 +294,16 @@ int dispatch_nt(const QArgs& a, int KS, size_t smem, cudaStream_t st) {
 
 int rows_per_cta(int M) { return (M > 32) ? 128 : 64; }
 
+// Rows up to which tiled INT4 GEMMs take the mma.sync GEMV (gemv.cu); ORCHARD_GEMV_MAX_M
+// overrides (0: always the tensor-core kernel).
+uint32_t gemv_tiled_limit() {
+  static const uint32_t v = [] {
+    const char* e = std::getenv("ORCHARD_GEMV_MAX_M");
+    return e ? (uint32_t)std::max(0, std::atoi(e)) : gemv_max_m();
+  }();
+  return std::min(v, gemv_max_m());
+}
+
 // CTAs per SM the cluster K-split aims for (more resident warps keep more weight bytes in
 // flight); ORCHARD_QGEMM_CTAS_PER_SM overrides.
 int ks_target() {
@@ -312,8 +322,12 @@ template <int WF, int EPI>
 int qgemm_run(QArgs a, cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0) return ORCH_OK;
   if (a.K <= 0 || (a.K % 32) != 0) return fail(ORCH_ERR_UNSUPPORTED, "K must be a positive multiple of 32");
-  if (a.tiled) {  // tiled INT4 weights: tensor-core path for every M
+  if (a.tiled) {  // tiled INT4 weights: GEMV kernel for a few rows, tensor-core kernel above
     if (WF != W_Q4) return fail(ORCH_ERR_INVALID, "tiled weights are INT4 only");
+    if (!a.x_f32 && a.M <= (int)gemv_tiled_limit()) {
+      const int rc = gemv_tiled_run<EPI>(a, st);
+      if (rc != ORCH_ERR_UNSUPPORTED) return rc;
+    }
     const int rc = tc_qgemm_run<EPI>(a, st);
     if (rc == ORCH_ERR_UNSUPPORTED)
       return fail(ORCH_ERR_UNSUPPORTED, "tiled INT4 GEMM: needs fp16 activations and 16-byte aligned buffers");

@@ -64,6 +64,10 @@ template <int EPI>
 int tc_qgemm_run(QArgs a, cudaStream_t st);
 // Activation-row count from which INT4 GEMMs take the tensor-core path (0 = never).
 uint32_t tc_min_m();
+// mma.sync GEMV on tiled weights for M <= gemv_max_m() (gemv.cu).
+template <int EPI>
+int gemv_tiled_run(QArgs a, cudaStream_t st);
+uint32_t gemv_max_m();
 
 namespace cg = cooperative_groups;
 

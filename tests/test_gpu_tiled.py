@@ -5,9 +5,15 @@
   [2 halves][128 rows][16 B] then the block's scales [8][128] fp16, nibbles of each word
   stored k0 k2 k4 k6 k1 k3 k5 k7, padding = nibble 8 / scale 0).
 * ``orch_q4t_gemm`` against the oracle (max|gpu - ref| / max|ref| <= 1e-2) and against the
-  reference-layout tensor-core GEMM (same arithmetic: <= 1e-6 of max|ref|).
-* The fused tiled entry points against the reference-layout ones (<= 1e-6).
+  reference-layout tensor-core GEMM: the same arithmetic for M > 8 (<= 1e-6 of max|ref|);
+  for M <= 8 the tiled path is the mma.sync GEMV, whose fp32 sums run in another order
+  (<= 2e-3, the kernel-to-kernel tolerance of the other GEMM tests).
+* The fused tiled entry points against the reference-layout ones (same tolerances).
 """
+
+
+def kernel_tol(M):
+    return 1e-6 if M > 8 else 2e-3
 
 import functools
 
@@ -109,7 +115,7 @@ def test_tiled_gemm_matches_oracle(K, N, M):
     ref = x.astype(np.float32) @ wd.T
     assert rel_err(y, ref) <= 1e-2
     if K % 256 == 0:
-        assert rel_err(y, gemm_ref_layout(p, s, x)) <= 1e-6
+        assert rel_err(y, gemm_ref_layout(p, s, x)) <= kernel_tol(M)
 
 
 def test_tiled_gemm_fp16_output():
@@ -173,7 +179,7 @@ def test_tiled_fused_match_reference_layout(M):
         torch.cuda.synchronize()
         outs.append([t.float().cpu().numpy() for t in (q, kc, vc, h, res)])
     for a, b in zip(*outs):
-        assert rel_err(a, b) <= 1e-6
+        assert rel_err(a, b) <= kernel_tol(M)
 
 
 def test_tiled_flag_clear_after_runs():
