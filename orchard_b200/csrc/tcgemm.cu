@@ -30,48 +30,13 @@
 #include <algorithm>
 #include <cstdlib>
 
+#include "async_copy.cuh"
 #include "qgemm.cuh"
 
 namespace orch {
 
 constexpr int kTcRows = 128;
 constexpr int kTcBK = 64;  // k per stage: one 128-byte swizzle row of fp16
-constexpr unsigned long long kWaitNs = 2000000000ull;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for the phase of `parity` to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = gtimer();
-  while (!mbar_try(bar, parity)) {
-    if (gtimer() - t0 > kWaitNs) return false;
-  }
-  return true;
-}
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -79,14 +44,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
-// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -174,19 +131,6 @@ __device__ __forceinline__ uint4 dq8_tiled(uint32_t w, uint32_t sc) {
   o.z = h2_bits(__hmul2(__hsub2(bits_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u)), magic_sub), s2));
   o.w = h2_bits(__hmul2(__hfma2(bits_h2(lop3_and_or(v, 0x00F000F0u, 0x64006400u)), hi_mul, hi_add), s2));
   return o;
-}
-
-// Bounded wait that also gives up as soon as another role of the CTA has failed.
-__device__ __forceinline__ bool mbar_wait_f(uint64_t* bar, uint32_t parity, volatile int* failed) {
-  if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = gtimer();
-  while (!mbar_try(bar, parity)) {
-    if (*failed || gtimer() - t0 > kWaitNs) return false;
-  }
-  return true;
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 constexpr int kWBytes = kTcRows * (kTcBK / 2);  // packed INT4 tile: 128 rows x 32 bytes

@@ -112,13 +112,17 @@ def main():
     ap.add_argument("--kernel", default="all", choices=["q4", "q4t", "q8pc", "attn", "all"])
     ap.add_argument("--M", default="1,16,64")
     ap.add_argument("--shape", default="", help="only this decode shape name (qkv, o, gate_up, down, lm_head)")
+    ap.add_argument("--shapes", default="", help="extra GEMM shapes K:N,K:N,... (timed instead of the decode shapes)")
     ap.add_argument("--reps", type=int, default=50)
     a = ap.parse_args()
     call("orch_init", 0, None)
     Ms = [int(v) for v in a.M.split(",")]
     for M in Ms:
         if a.kernel in ("q4", "q4t", "q8pc", "all"):
-            for name, K, N in DECODE_SHAPES:
+            shapes = DECODE_SHAPES
+            if a.shapes:
+                shapes = [(f"{k}x{n}", int(k), int(n)) for k, n in (v.split(":") for v in a.shapes.split(","))]
+            for name, K, N in shapes:
                 if a.shape and name != a.shape:
                     continue
                 for fmt in (("q4t", "q4", "q8pc") if a.kernel == "all" else (a.kernel,)):
