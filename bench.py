@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--extra-batches", default="1,16", help="also time these batch sizes (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-column-split", action="store_true", help="at N > 1 skip the column-split measurement")
     ap.add_argument("--layers", type=int, default=32)
     return ap.parse_args()
 
@@ -104,7 +105,7 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------
 # model construction (random init on the device, packed with the reference rule)
 # ------------------------------------------------------------------------------------------------
-def build_model(cfg, device, max_batch, seed=1234):
+def build_model(cfg, device, max_batch, seed=1234, group=None):
     import torch
 
     from orchard_b200 import loader
@@ -130,7 +131,7 @@ def build_model(cfg, device, max_batch, seed=1234):
     ck.embed = torch.randn((V, H), generator=gen, device=device).half()
     ck.norm = (1 + 0.1 * torch.randn(H, generator=gen, device=device)).half().float().cpu().numpy()
     ck.lm_head = packed(V, H)
-    return Llama(checkpoint=ck, device=device, max_batch=max_batch, max_seq=MAX_SEQ)
+    return Llama(checkpoint=ck, device=device, max_batch=max_batch, max_seq=MAX_SEQ, group=group)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -260,6 +261,35 @@ def time_prefill_lora(llm, reps=3, seqs=8, length=512, rank=16, seed=11):
             "tok_s": round(tokens / t, 1), "tflops": round(flops / t / 1e12, 2), "flops": flops}
 
 
+def time_column_split(cfg, dev, global_batch, steps, warmup, rank, world):
+    """The column split (sequences sharded, FFN and vocabulary projections split by columns,
+    two NCCL collectives per layer): global_batch sequences, global_batch / world per rank,
+    512-token prompts, greedy decode steps timed on the device (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    B = global_batch // world
+    llm = build_model(cfg, dev, B, seed=4321, group=dist.group.WORLD)  # same weights on every rank
+    eng = llm.engine
+    g = np.random.default_rng([20261201, 6, rank])
+    llm.prefill(g.integers(0, cfg["vocab_size"], (B, PROMPT)).tolist())
+    start = PROMPT + 3 - warmup if warmup <= 3 else PROMPT
+    eng.pos[:B].fill_(PROMPT)
+    eng.step(B, logits=True)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    secs = time_decode(llm, B, steps, warmup, start)
+    t = torch.tensor([secs], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    eng.release_graphs()
+    del llm, eng
+    torch.cuda.empty_cache()
+    secs = float(t.item())
+    return {"global_batch": global_batch, "per_rank_batch": B, "steps": steps,
+            "tok_s": round(global_batch * steps / secs, 2), "ms_per_step": round(secs / steps * 1000, 4),
+            "collectives_per_layer": 2, "note": "FFN and lm_head column-split over NCCL; attention data-parallel"}
+
+
 def cpu_baseline_sample(B, target_s=15.0):
     """The oracle's decode step on the host cores: a 2-layer 7B-shape slice at batch B with
     577 cached positions, scaled by 16 to 32 layers (+ the lm_head once)."""
@@ -319,9 +349,10 @@ def run_ours(args):
     import torch.distributed as dist
 
     rank, world, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
     torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     cfg = dict(CFG7B, num_hidden_layers=args.layers)
     B = args.batch
@@ -389,6 +420,13 @@ def run_ours(args):
             "gpu_launches": eng.kernel_launches_per_step(B) * args.steps}
     if rank == 0:
         line["clocks"] = clk.summary()
+    # the column split, measured beside the replicas (N > 1)
+    if world > 1 and not args.no_column_split:
+        del llm, eng
+        torch.cuda.empty_cache()
+        line["column_split"] = time_column_split(cfg, dev, B, min(args.steps, 32), args.warmup, rank, world)
+        llm = build_model(cfg, dev, max_b, seed=1234 + rank)
+        eng = llm.engine
     # per-batch lines (N = 1 only)
     if world == 1:
         per = {}

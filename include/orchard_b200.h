@@ -201,6 +201,16 @@ int orch_attention_decode(const void* q, const void* k_cache, const void* v_cach
  * kernel (TMEM accumulators, TMA-fed activations); fewer rows use the mma.sync decode
  * kernel. 0 disables the tensor-core kernel. Default 17 (ORCHARD_TC_MIN_M overrides). */
 int orch_set_tc_min_m(uint32_t m);
+/* Vocabulary-split greedy sampling (no reference counterpart: the reference samples on the
+ * host, orchard/model.py:244-252). orch_argmax_pairs writes, per row of a logits slice
+ * [M, V] whose first column is vocabulary id `base`, the pair (max logit, base + argmax)
+ * as floats; orch_argmax_merge reduces the all-gathered pairs [world][B][2] of rows
+ * row0 .. row0 + rows - 1 to token ids: the highest logit, the lowest id among equal
+ * logits, a NaN first (np.argmax over the whole vocabulary). */
+int orch_argmax_pairs(const float* logits, uint32_t M, uint32_t V, uint32_t base, float* pairs,
+                      void* stream);
+int orch_argmax_merge(const float* pairs, uint32_t world, uint32_t B, uint32_t row0, uint32_t rows,
+                      int32_t* tok, void* stream);
 /* Decode attention that allocates nothing (no counterpart in the reference). Same inputs,
  * outputs and arithmetic as orch_attention_decode, but the split-position partials live in
  * a 1 MiB array inside the library (orch_attention_noalloc_max_bytes()) that every GPU

@@ -215,7 +215,10 @@ __global__ void softmax_rows_kernel(const TI* in, TO* out, int cols) {
 }
 
 // ---- row argmax (first index of the maximum, as np.argmax) ---------------------------------
-__global__ void argmax_rows_kernel(const float* logits, int V, int* out) {
+// PAIRS: also write the row's maximum (as float) and base + index (as float, exact below
+// 2^24) to out_pairs[row] for the vocabulary-split merge.
+template <bool PAIRS>
+__global__ void argmax_rows_kernel(const float* logits, int V, int* out, float2* out_pairs, int base) {
   __shared__ float sv[32];
   __shared__ int si[32];
   pdl_trigger();
@@ -258,7 +261,13 @@ __global__ void argmax_rows_kernel(const float* logits, int V, int* out) {
         bi = oi;
       }
     }
-    if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    if (lane == 0) {
+      const int i = bi == 0x7fffffff ? 0 : bi;
+      if (PAIRS)
+        out_pairs[blockIdx.x] = make_float2(best, (float)(base + i));
+      else
+        out[blockIdx.x] = i;
+    }
   }
 }
 
@@ -332,9 +341,47 @@ extern "C" int orch_softmax(const void* in, void* out, uint32_t rows, uint32_t c
 extern "C" int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, void* stream) {
   if (M == 0) return ORCH_OK;
   ORCH_REQUIRE(logits && out && V > 0, "argmax_rows: bad arguments");
-  ORCH_CUDA(launch_k(argmax_rows_kernel, dim3(M), dim3(1024), 0, as_stream(stream), dim3(0, 0, 0), logits,
-                     (int)V, (int*)out));
+  ORCH_CUDA(launch_k(argmax_rows_kernel<false>, dim3(M), dim3(1024), 0, as_stream(stream), dim3(0, 0, 0), logits,
+                     (int)V, (int*)out, (float2*)nullptr, 0));
   return check_launch("argmax_rows");
+}
+
+// (max, base + argmax) of each row of a vocabulary slice, as float pairs [M][2].
+extern "C" int orch_argmax_pairs(const float* logits, uint32_t M, uint32_t V, uint32_t base, float* pairs,
+                                 void* stream) {
+  if (M == 0) return ORCH_OK;
+  ORCH_REQUIRE(logits && pairs && V > 0 && base + V < (1u << 24), "argmax_pairs: bad arguments");
+  ORCH_CUDA(launch_k(argmax_rows_kernel<true>, dim3(M), dim3(1024), 0, as_stream(stream), dim3(0, 0, 0), logits,
+                     (int)V, (int*)nullptr, (float2*)pairs, (int)base));
+  return check_launch("argmax_pairs");
+}
+
+namespace orch {
+// One thread per row: the highest value over the ranks' pairs, the lowest id among equal
+// values, a NaN wins (np.argmax over the whole vocabulary).
+__global__ void argmax_merge_kernel(const float2* pairs, int world, int B, int row0, int rows, int* tok) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float2 best = pairs[row0 + r];
+  for (int w = 1; w < world; ++w) {
+    if (best.x != best.x) break;
+    const float2 v = pairs[(size_t)w * B + row0 + r];
+    if (v.x != v.x || v.x > best.x || (v.x == best.x && v.y < best.y)) best = v;
+  }
+  tok[r] = (int)best.y;
+}
+}  // namespace orch
+
+// Merge the all-gathered pairs [world][B][2] for rows row0 .. row0 + rows - 1 into tokens.
+extern "C" int orch_argmax_merge(const float* pairs, uint32_t world, uint32_t B, uint32_t row0, uint32_t rows,
+                                 int32_t* tok, void* stream) {
+  if (rows == 0) return ORCH_OK;
+  ORCH_REQUIRE(pairs && tok && world > 0 && row0 + rows <= B, "argmax_merge: bad arguments");
+  ORCH_CUDA(launch_k(argmax_merge_kernel, dim3((rows + 127) / 128), dim3(128), 0, as_stream(stream),
+                     dim3(0, 0, 0), (const float2*)pairs, (int)world, (int)B, (int)row0, (int)rows, (int*)tok));
+  return check_launch("argmax_merge");
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -35,6 +35,7 @@ import torch
 from . import _lib
 from ._lib import F16, F32, call, ptr
 from .loader import Checkpoint, from_tensors, load_checkpoint, load_lora
+from .parallel import ColumnSplit, ffn_column_split, head_column_split
 
 EOS_ID = 2
 
@@ -143,9 +144,14 @@ class DeviceLayer:
     the tiled layout (`tiled`, the default: tcgen05 GEMM for every row count) or in the
     reference layout (mma.sync GEMV below the tensor-core threshold)."""
 
-    def __init__(self, entries: dict, cfg: LlamaConfig, device, tiled: bool = True):
+    def __init__(self, entries: dict, cfg: LlamaConfig, device, tiled: bool = True,
+                 split: Optional[ColumnSplit] = None):
         H, F = cfg.hidden_size, cfg.intermediate_size
         q = {n: _packed_on_device(entries[n], device) for n in ("wq", "wk", "wv", "wo", "w1", "w3", "w2")}
+        if split is not None:  # this rank's FFN columns: gate/up rows f0:f1, down columns f0:f1
+            w1, s1, w3, s3, w2, s2 = split.ffn_shard(*q["w1"], *q["w3"], *q["w2"])
+            q["w1"], q["w3"], q["w2"] = (w1, s1), (w3, s3), (w2.contiguous(), s2.contiguous())
+            F = split.f_local
         self.wqkv = torch.cat([q["wq"][0], q["wk"][0], q["wv"][0]]).contiguous()
         self.sqkv = torch.cat([q["wq"][1], q["wk"][1], q["wv"][1]]).contiguous()
         self.wo, self.so = q["wo"]
@@ -156,6 +162,7 @@ class DeviceLayer:
         self.ffn_norm = torch.as_tensor(np.asarray(entries["ffn_norm"], np.float32)).to(device)
         assert self.wqkv.shape == (3 * H, H // 2) and self.w13.shape == (2 * F, H // 2)
         assert self.w2.shape == (H, F // 2)
+        self.f_local = F
         self.tiled = tiled
         if tiled:
             self.tqkv = tile_q4(self.wqkv, self.sqkv)
@@ -222,11 +229,86 @@ class RowBuffers:
         self.attn_ws_bytes = ws
 
 
+class _SplitBuffers:
+    """Buffers of the column-split FFN and head for up to ``rb.rows`` local rows: the
+    gathered rows of every rank (rank-major), this rank's FFN slice of them, the fp32
+    partial down projection and its reduced local rows, the vocabulary slice's logits and
+    the (max, id) pairs."""
+
+    def __init__(self, rb: RowBuffers, split: ColumnSplit, cfg: "LlamaConfig", device):
+        H = cfg.hidden_size
+        W, R = split.world, rb.rows
+        self.x, self.xn, self.tok = rb.x, rb.xn, rb.tok_out
+        self.xn_all = torch.zeros((W * R, H), dtype=torch.float16, device=device)
+        self.h = torch.zeros((W * R, split.f_local), dtype=torch.float16, device=device)
+        self.part = torch.zeros((W * R, H), dtype=torch.float32, device=device)
+        self.red = torch.zeros((R, H), dtype=torch.float32, device=device)
+        self.logits = torch.zeros((W * R, split.v_local), dtype=torch.float32, device=device)
+        self.pairs = torch.zeros((W * R, 2), dtype=torch.float32, device=device)
+        self.pairs_all = torch.zeros((W * W * R, 2), dtype=torch.float32, device=device)
+
+
+class _CudaSplitOps:
+    """The column split's kernels on this rank (parallel.py names the order)."""
+
+    def __init__(self, eng: "DecodeEngine"):
+        self.e = eng
+
+    def rmsnorm(self, x, w, xn, rows):
+        c = self.e.cfg
+        call("orch_rmsnorm_ex", ptr(x), F32, ptr(self.e.norm if w is None else w), F32, ptr(xn), F16,
+             c.rms_norm_eps, c.hidden_size, rows, _stream())
+
+    def gate_up_swiglu(self, layer, xn_all, h, rows):
+        call("orch_q4t_linear_swiglu", ptr(layer.t13), ptr(xn_all), ptr(h), rows, self.e.cfg.hidden_size,
+             layer.f_local, None, None, 0, _stream())
+
+    def down_partial(self, layer, h, part, rows):
+        call("orch_q4t_gemm", ptr(layer.t2), ptr(h), ptr(part), F32, layer.f_local, self.e.cfg.hidden_size, rows,
+             _stream())
+
+    def add(self, x, red, rows):
+        call("orch_binary_ex", 0, ptr(x), ptr(red), ptr(x), F32, rows * self.e.cfg.hidden_size, _stream())
+
+    def lm_partial(self, xn_all, logits, rows):
+        sp = self.e.split
+        call("orch_q4t_gemm", ptr(self.e.lm_t), ptr(xn_all), ptr(logits), F32, self.e.cfg.hidden_size, sp.v_local,
+             rows, _stream())
+
+    def argmax_pairs(self, logits, pairs, rows):
+        sp = self.e.split
+        call("orch_argmax_pairs", ptr(logits), rows, sp.v_local, sp.v0, ptr(pairs), _stream())
+
+    def merge_pairs(self, pairs_all, tok, rows):
+        sp = self.e.split
+        call("orch_argmax_merge", ptr(pairs_all), sp.world, sp.world * rows, sp.rank * rows, rows, ptr(tok),
+             _stream())
+
+
+class _NcclComm:
+    """Collectives of the column split over a torch.distributed (NCCL) group; buffers are
+    row-major, the first ``rows`` rows of the input and ``world * rows`` of the output."""
+
+    def __init__(self, group, world: int):
+        self.group, self.world = group, world
+
+    def all_gather(self, out, inp, rows):
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(out[:self.world * rows], inp[:rows], group=self.group)
+
+    def reduce_scatter(self, out, inp, rows):
+        import torch.distributed as dist
+        dist.reduce_scatter_tensor(out[:rows], inp[:self.world * rows], op=dist.ReduceOp.SUM, group=self.group)
+
+
 class DecodeEngine:
-    """Device state for up to ``max_batch`` sequences of up to ``max_seq`` positions."""
+    """Device state for up to ``max_batch`` sequences of up to ``max_seq`` positions.
+    With ``group`` (a torch.distributed NCCL group of several ranks, one GPU each) the
+    sequences are sharded over the ranks and the FFN and vocabulary projections are split
+    by columns (parallel.py); ``M`` then counts this rank's rows, equal on every rank."""
 
     def __init__(self, ck: Checkpoint, device=0, max_batch: int = 32, max_seq: Optional[int] = None,
-                 tiled: bool = True):
+                 tiled: bool = True, group=None):
         if not torch.cuda.is_available():
             raise RuntimeError("orchard_b200 needs a CUDA device (there is no CPU fallback)")
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
@@ -241,13 +323,27 @@ class DecodeEngine:
         self.max_pos = max(self.max_seq, cfg.max_position_embeddings)
         dev = self.device
         self.tiled = tiled
-        self.layers = [DeviceLayer(e, cfg, dev, tiled) for e in ck.layers]
+        # column split over the ranks of `group` (torch.distributed, NCCL): sequences sharded,
+        # FFN and vocabulary projections split by columns (parallel.py)
+        self.group = group
+        self.split: Optional[ColumnSplit] = None
+        if group is not None:
+            import torch.distributed as dist
+            world, rank = dist.get_world_size(group), dist.get_rank(group)
+            if world > 1:
+                if not tiled:
+                    raise ValueError("the column split runs on tiled weights")
+                self.split = ColumnSplit.plan(F, V, world, rank)
+        self.layers = [DeviceLayer(e, cfg, dev, tiled, self.split) for e in ck.layers]
         emb = ck.embed if isinstance(ck.embed, torch.Tensor) else torch.as_tensor(np.asarray(ck.embed))
         if emb.dtype not in (torch.float16, torch.float32):
             emb = emb.float()
         self.embed = emb.to(dev).contiguous()
         self.norm = torch.as_tensor(np.asarray(ck.norm, np.float32)).to(dev)
         self.lm_w, self.lm_s = _packed_on_device(ck.lm_head, dev)
+        if self.split is not None:
+            w, sc = self.split.lm_shard(self.lm_w, self.lm_s)
+            self.lm_w, self.lm_s = w.contiguous(), sc.contiguous()
         if tiled:
             self.lm_t = tile_q4(self.lm_w, self.lm_s)
             torch.cuda.current_stream().synchronize()
@@ -256,11 +352,20 @@ class DecodeEngine:
         self.cos = torch.as_tensor(cos).to(dev)
         self.sin = torch.as_tensor(sin).to(dev)
         nl, nh, hd = cfg.num_hidden_layers, cfg.num_attention_heads, cfg.head_dim
-        self.k_cache = torch.zeros((nl, max_batch, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
+        # with the column split one extra slot takes the padding rows of a prefill whose
+        # token count is below another rank's (their K/V land there and are never read)
+        self.scratch_slot = max_batch if self.split is not None else -1
+        nslots = max_batch + (1 if self.split is not None else 0)
+        self.k_cache = torch.zeros((nl, nslots, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.lora_r = 0
-        self.dec = RowBuffers(max_batch, cfg, self.max_seq, dev, logits=True)
+        self.dec = RowBuffers(max_batch, cfg, self.max_seq, dev, logits=self.split is None)
         self.pre: Optional[RowBuffers] = None
+        self.sdec = _SplitBuffers(self.dec, self.split, cfg, dev) if self.split is not None else None
+        self.spre: Optional[_SplitBuffers] = None
+        if self.split is not None:
+            self._split_ops = _CudaSplitOps(self)
+            self._comm = _NcclComm(group, self.split.world)
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         torch.cuda.synchronize(dev)
 
@@ -320,6 +425,12 @@ class DecodeEngine:
             else:
                 call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
             call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.ffn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
+            if self.split is not None:
+                if "gu" in L.lora or "down" in L.lora:
+                    raise ValueError("LoRA on the FFN projections is not supported with the column split")
+                sb = self.sdec if b is self.dec else self._split_bufs(b)
+                ffn_column_split(self._split_ops, self._comm, L, sb, M)
+                continue
             lt, lb, lr = self._lora(L, "gu", b.xn, M, s, b)
             if L.tiled:
                 call("orch_q4t_linear_swiglu", ptr(L.t13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
@@ -336,6 +447,9 @@ class DecodeEngine:
         b = self.dec
         cfg, s = self.cfg, _stream()
         H, V = cfg.hidden_size, cfg.vocab_size
+        if self.split is not None:
+            head_column_split(self._split_ops, self._comm, self.sdec, M)
+            return
         call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(self.norm), F32, ptr(b.xn), F16, cfg.rms_norm_eps, H, M, s)
         if self.tiled:
             call("orch_q4t_gemm", ptr(self.lm_t), ptr(b.xn), ptr(b.logits), F32, H, V, M, s)
@@ -350,6 +464,17 @@ class DecodeEngine:
         projections take the tensor-core GEMM; attention is causal per row (each row attends
         to positions 0..pos of its slot, written by this or an earlier chunk)."""
         n = len(tokens)
+        if self.split is not None:
+            # every rank runs the same chunks (the FFN collectives): pad to the largest count
+            import torch.distributed as dist
+            cnt = torch.tensor([n], dtype=torch.int64, device=self.device)
+            dist.all_reduce(cnt, op=dist.ReduceOp.MAX, group=self.group)
+            pad = int(cnt.item()) - n
+            if pad:
+                tokens = np.concatenate([np.asarray(tokens, np.int32), np.zeros(pad, np.int32)])
+                positions = np.concatenate([np.asarray(positions, np.int32), np.zeros(pad, np.int32)])
+                slots = np.concatenate([np.asarray(slots, np.int32), np.full(pad, self.scratch_slot, np.int32)])
+                n += pad
         if n == 0:
             return
         rows = min(chunk, n)
@@ -366,14 +491,21 @@ class DecodeEngine:
             b.slots[:m].copy_(s_d[r0:r0 + m])
             self.run_layers(m, b)
 
+    def _split_bufs(self, b: RowBuffers) -> _SplitBuffers:
+        if self.spre is None or self.spre.x is not b.x:
+            self.spre = _SplitBuffers(b, self.split, self.cfg, self.device)
+        return self.spre
+
     def kernel_launches_per_step(self, M: int, logits: bool = True) -> int:
         """Kernels of this library one step launches (for reporting)."""
         per_layer = 7 + sum(1 for L in self.layers[:1] for _ in L.lora)
+        if self.split is not None:
+            per_layer += 1  # the residual add after the reduce-scatter
         n = 1 + per_layer * len(self.layers)
         if _lib.lib().orch_attention_workspace_bytes(M, self.cfg.num_attention_heads, self.cfg.head_dim,
                                                      self.max_seq) > 0:
             n += len(self.layers)
-        return n + (3 if logits else 0)
+        return n + ((4 if self.split is not None else 3) if logits else 0)
 
     def step(self, M: int, logits: bool = True, graph: bool = True):
         """One decode (or prefill) step for rows [0, M); with `graph` the step is replayed
@@ -404,6 +536,12 @@ class DecodeEngine:
             # capture only records; the step itself still has to run
         g.replay()
 
+    def release_graphs(self):
+        """Drops the captured steps (those of a column split hold NCCL calls and must go
+        before the process group is destroyed)."""
+        self.graphs.clear()
+        torch.cuda.synchronize(self.device)
+
     def reset_cache(self):
         self.k_cache.zero_()
         self.v_cache.zero_()
@@ -418,10 +556,11 @@ class Llama:
 
     def __init__(self, model_path: Optional[str] = None, *, checkpoint: Optional[Checkpoint] = None,
                  device=0, max_batch: int = 32, max_seq: Optional[int] = None, tokenizer=None,
-                 use_graphs: bool = True, tiled: bool = True):
+                 use_graphs: bool = True, tiled: bool = True, group=None):
         ck = checkpoint if checkpoint is not None else load_checkpoint(model_path)
         self.config = dict(ck.config)
-        self.engine = DecodeEngine(ck, device=device, max_batch=max_batch, max_seq=max_seq, tiled=tiled)
+        self.engine = DecodeEngine(ck, device=device, max_batch=max_batch, max_seq=max_seq, tiled=tiled,
+                                   group=group)
         self.use_graphs = use_graphs
         self.tokenizer = tokenizer
         if tokenizer is None and model_path is not None:
@@ -489,6 +628,8 @@ class Llama:
 
         eng = self.engine
         B = len(prompt_ids)
+        if eng.split is not None and temperature != 0:
+            raise ValueError("the column split samples greedily on the device (temperature 0)")
         lens = np.array([len(p) for p in prompt_ids], np.int32)
         total = int(lens.max()) + max_tokens
         if total > eng.max_seq:
@@ -520,7 +661,7 @@ class Llama:
         for step in range(max_tokens):
             if greedy and step >= 1:
                 consume(step - 1)
-            if not active.any():
+            if not active.any() and eng.split is None:  # split ranks stay in step together
                 break
             eng.pos[:B].copy_(pos_host[step], non_blocking=True)
             eng.step(B, logits=True, graph=self.use_graphs)

@@ -1,0 +1,76 @@
+"""The column split on two GPUs (skipped with fewer): two ranks (NCCL) each own one of the
+tiny checkpoint's two sequences and half of its FFN and vocabulary columns; greedy
+``generate_batch_ids`` on each rank must reproduce the tokens the reference's own
+``orchard/model.py`` produced for that sequence (tests/golden/tiny_model.npz), with the
+decode step captured in CUDA graphs and eagerly. The prompts have different lengths, so
+the shorter rank's prefill is padded into the scratch slot."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tiny_model.npz")
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, graphs, q):
+    import datetime
+    import json
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    llm = None
+    try:
+        from orchard_b200.model import Llama
+        z = np.load(GOLDEN)
+        cfg = json.loads(str(z["config_json"]))
+        ckpt = {k[len("ckpt/"):]: z[k] for k in z.files if k.startswith("ckpt/")}
+        prompts = [[int(v) for v in p if v >= 0] for p in z["prompts"]]
+        llm = Llama.from_tensors(cfg, ckpt, device=rank, max_batch=2, use_graphs=graphs, group=dist.group.WORLD)
+        toks = llm.generate_batch_ids([prompts[rank]], max_tokens=int(z["max_tokens"]), temperature=0)
+        q.put((rank, toks[0], None))
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, repr(e)))
+    finally:
+        if llm is not None:
+            llm.engine.release_graphs()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("graphs", [True, False])
+def test_column_split_two_gpus_matches_reference_golden(graphs):
+    import torch.multiprocessing as mp
+    z = np.load(GOLDEN)
+    ref = [[int(v) for v in t if v >= 0] for t in z["tokens"]]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, graphs, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, t, err = q.get(timeout=300)
+        assert err is None, err
+        got[r] = t
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert [got[0], got[1]] == ref

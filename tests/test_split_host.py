@@ -1,0 +1,216 @@
+"""Host logic of the multi-GPU column split (CPU; two gloo ranks for the collectives).
+
+The split plan (which FFN / vocabulary columns a rank holds), the merge of per-rank
+(max, id) pairs, and the order of operations in ``parallel.ffn_column_split`` /
+``head_column_split`` are checked here with NumPy kernels built on the oracle: two ranks
+each hold half of the FFN columns and half of the vocabulary, and their result must equal
+the unsplit computation (fp32 sums split in K: max-rel <= 1e-5; tokens exact).
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import ops
+from orchard_b200.parallel import ColumnSplit, ffn_column_split, head_column_split, local_rows, merge_argmax, shard_range
+
+
+@pytest.mark.parametrize("n,world,align", [(11008, 2, 32), (11008, 4, 32), (11008, 8, 32), (32000, 8, 16),
+                                           (4096, 8, 32), (100, 3, 16), (64, 2, 16)])
+def test_shard_range_covers_and_aligns(n, world, align):
+    spans = [shard_range(n, world, r, align) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0
+    for lo, hi in spans:
+        assert lo % align == 0 and (hi % align == 0 or hi == n)
+        assert hi > lo
+    sizes = [hi - lo for lo, hi in spans]
+    assert max(sizes) - min(sizes) <= align
+
+
+def test_plan_7b_shapes():
+    for world in (2, 4, 8):
+        parts = [ColumnSplit.plan(11008, 32000, world, r) for r in range(world)]
+        assert sum(p.f_local for p in parts) == 11008 and sum(p.v_local for p in parts) == 32000
+        assert all(p.f_local % 32 == 0 for p in parts)  # down-projection K slices start on a group
+        assert all(p.f_local % 16 == 0 for p in parts)  # gate/up interleave blocks
+    assert ColumnSplit.plan(11008, 32000, 8, 0).f_local == 1376
+
+
+def test_local_rows():
+    assert local_rows(64, 8, 3) == (24, 32)
+    with pytest.raises(ValueError):
+        local_rows(10, 4, 0)
+
+
+def test_merge_argmax_matches_np_argmax():
+    g = np.random.default_rng(3)
+    world, B, per = 4, 50, 7
+    logits = g.integers(-3, 3, (B, world * per)).astype(np.float32)  # many ties
+    logits[5, 9] = np.nan
+    logits[6, 20] = np.nan
+    logits[6, 3] = np.nan
+    vals = np.empty((world, B), np.float32)
+    idx = np.empty((world, B), np.int64)
+    for r in range(world):
+        sl = logits[:, r * per:(r + 1) * per]
+        i = np.argmax(sl, axis=1)
+        vals[r] = sl[np.arange(B), i]
+        idx[r] = r * per + i
+    assert np.array_equal(merge_argmax(vals, idx), np.argmax(logits, axis=1))
+
+
+# ------------------------------------------------------------------------------------------
+# two gloo ranks running the split orchestration with oracle kernels
+# ------------------------------------------------------------------------------------------
+
+H, F, V, B, EPS = 64, 192, 64, 4, 1e-5
+
+
+def model(seed=11):
+    g = np.random.default_rng(seed)
+
+    def q(n, k):
+        return ops.quantize_q4_0((g.standard_normal((n, k)) * 0.05).astype(np.float32))
+
+    return {"w1": q(F, H), "w3": q(F, H), "w2": q(H, F), "lm": q(V, H),
+            "ffn_norm": (1 + 0.1 * g.standard_normal(H)).astype(np.float32),
+            "norm": (1 + 0.1 * g.standard_normal(H)).astype(np.float32),
+            "x": g.standard_normal((B, H)).astype(np.float32)}
+
+
+class NpOps:
+    """The ops interface of parallel.py with oracle arithmetic on CPU tensors."""
+
+    def __init__(self, m, plan):
+        self.m, self.p = m, plan
+        w1, s1, w3, s3, w2, s2 = plan.ffn_shard(*m["w1"], *m["w3"], *m["w2"])
+        self.w1 = ops.dequantize_q4_0(w1, s1)
+        self.w3 = ops.dequantize_q4_0(w3, s3)
+        self.w2 = ops.dequantize_q4_0(np.ascontiguousarray(w2), np.ascontiguousarray(s2))
+        self.lm = ops.dequantize_q4_0(*plan.lm_shard(*m["lm"]))
+
+    def rmsnorm(self, x, w, xn, rows):
+        w = self.m["norm"] if w is None else w
+        xn[:rows] = torch.from_numpy(ops.rmsnorm(x[:rows].numpy(), w, EPS).astype(np.float16))
+
+    def gate_up_swiglu(self, layer, xn_all, h, rows):
+        a = xn_all[:rows].float().numpy()
+        h[:rows] = torch.from_numpy((ops.silu(a @ self.w1.T) * (a @ self.w3.T)).astype(np.float16))
+
+    def down_partial(self, layer, h, part, rows):
+        part[:rows] = torch.from_numpy(h[:rows].float().numpy() @ self.w2.T)
+
+    def add(self, x, red, rows):
+        x[:rows] += red[:rows]
+
+    def lm_partial(self, xn_all, logits, rows):
+        logits[:rows] = torch.from_numpy(xn_all[:rows].float().numpy() @ self.lm.T)
+
+    def argmax_pairs(self, logits, pairs, rows):
+        lg = logits[:rows].numpy()
+        i = np.argmax(lg, axis=1)
+        pairs[:rows, 0] = torch.from_numpy(lg[np.arange(rows), i])
+        pairs[:rows, 1] = torch.from_numpy((self.p.v0 + i).astype(np.float32))
+
+    def merge_pairs(self, pairs_all, tok, rows):
+        pa = pairs_all[:self.p.world * self.p.world * rows].numpy().reshape(self.p.world, self.p.world * rows, 2)
+        t = merge_argmax(pa[..., 0], pa[..., 1].astype(np.int64))
+        tok[:rows] = torch.from_numpy(t[self.p.rank * rows:(self.p.rank + 1) * rows].astype(np.int32))
+
+
+class GlooComm:
+    """all_gather / reduce_scatter on CPU tensors (the reduce-scatter as an all-reduce of
+    the whole buffer and a slice: same result)."""
+
+    def __init__(self, world, rank):
+        self.world, self.rank = world, rank
+
+    def all_gather(self, out, inp, rows):
+        parts = [torch.empty_like(inp[:rows]) for _ in range(self.world)]
+        dist.all_gather(parts, inp[:rows].contiguous())
+        out[:self.world * rows] = torch.cat(parts)
+
+    def reduce_scatter(self, out, inp, rows):
+        full = inp[:self.world * rows].clone()
+        dist.all_reduce(full)
+        out[:rows] = full[self.rank * rows:(self.rank + 1) * rows]
+
+
+class Bufs:
+    def __init__(self, plan, x_local):
+        W, R = plan.world, x_local.shape[0]
+        self.x = x_local.clone()
+        self.xn = torch.zeros((R, H), dtype=torch.float16)
+        self.xn_all = torch.zeros((W * R, H), dtype=torch.float16)
+        self.h = torch.zeros((W * R, plan.f_local), dtype=torch.float16)
+        self.part = torch.zeros((W * R, H), dtype=torch.float32)
+        self.red = torch.zeros((R, H), dtype=torch.float32)
+        self.logits = torch.zeros((W * R, plan.v_local), dtype=torch.float32)
+        self.pairs = torch.zeros((W * R, 2), dtype=torch.float32)
+        self.pairs_all = torch.zeros((W * W * R, 2), dtype=torch.float32)
+        self.tok = torch.zeros(R, dtype=torch.int32)
+
+
+class Layer:
+    def __init__(self, m):
+        self.ffn_norm = m["ffn_norm"]
+
+
+def _rank(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m = model()
+        plan = ColumnSplit.plan(F, V, world, rank)
+        r0, r1 = local_rows(B, world, rank)
+        bufs = Bufs(plan, torch.from_numpy(m["x"][r0:r1]))
+        o, c = NpOps(m, plan), GlooComm(world, rank)
+        ffn_column_split(o, c, Layer(m), bufs, r1 - r0)
+        x_after = bufs.x.numpy().copy()
+        head_column_split(o, c, bufs, r1 - r0)
+        q.put((rank, x_after, bufs.tok.numpy().copy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_column_split_two_gloo_ranks_match_unsplit():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, x, t = q.get(timeout=120)
+        res[r] = (x, t)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # unsplit reference
+    m = model()
+    d = {k: ops.dequantize_q4_0(*m[k]) for k in ("w1", "w3", "w2", "lm")}
+    xn = ops.rmsnorm(m["x"], m["ffn_norm"], EPS).astype(np.float16).astype(np.float32)
+    h = (ops.silu(xn @ d["w1"].T) * (xn @ d["w3"].T)).astype(np.float16).astype(np.float32)
+    x_ref = m["x"] + h @ d["w2"].T
+    xn2 = ops.rmsnorm(x_ref, m["norm"], EPS).astype(np.float16).astype(np.float32)
+    tok_ref = np.argmax(xn2 @ d["lm"].T, axis=1)
+    x_split = np.concatenate([res[r][0] for r in range(world)])
+    tok_split = np.concatenate([res[r][1] for r in range(world)])
+    assert np.abs(x_split - x_ref).max() / np.abs(x_ref).max() <= 1e-5
+    assert np.array_equal(tok_split, tok_ref)
