@@ -33,7 +33,6 @@ struct AttnArgs {
 
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
-  __shared__ __align__(16) float qs[HD];
   __shared__ float sc[kAttnChunk];
   __shared__ float red[32];
   __shared__ float accs[kAttnThreads / 32][HD];
@@ -58,36 +57,63 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   const __half* V = a.vc + base;
   const float scale = rsqrtf((float)HD);
 
-  for (int d = threadIdx.x; d < HD; d += kAttnThreads)
-    qs[d] = __half2float(a.q[(size_t)m * a.nh * HD + h * HD + d]) * scale;
-  __syncthreads();
-
-  // pass 1: one position per thread, full-row dot product (row = HD halves); the whole
-  // row is requested before it is used, and q comes from shared memory as float4
-  const float4* q4 = reinterpret_cast<const float4*>(qs);
-  float lmax = -INFINITY;
-  for (int t = p0 + threadIdx.x; t < p1; t += kAttnThreads) {
-    const __half* kr = K + (size_t)t * HD;
-    uint4 raw[HD / 8];
+  // pass 1: four lanes per position, each holding HD/4 dims of q (scaled) in registers; a
+  // warp scores 8 positions per step (a two-step shuffle sums the four partial dots), two
+  // steps' K rows are requested before either is used
+  constexpr int DPL = HD / 4, CPL = DPL / 8;  // dims and 16-byte chunks per lane
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane & 3;
+  float qv[DPL];
+  {
+    const __half* qp = a.q + (size_t)m * a.nh * HD + h * HD + sub * DPL;
 #pragma unroll
-    for (int v = 0; v < HD / 8; ++v) raw[v] = ld_stream16(kr + v * 8);
-    float s = 0.f;
+    for (int cidx = 0; cidx < CPL; ++cidx) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qp) + cidx);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-    for (int v = 0; v < HD / 8; ++v) {
-      const float4 qa = q4[2 * v], qb = q4[2 * v + 1];
-      const float2 f0 = __half22float2(bits_h2(raw[v].x)), f1 = __half22float2(bits_h2(raw[v].y));
-      const float2 f2 = __half22float2(bits_h2(raw[v].z)), f3 = __half22float2(bits_h2(raw[v].w));
-      s = fmaf(f0.x, qa.x, s);
-      s = fmaf(f0.y, qa.y, s);
-      s = fmaf(f1.x, qa.z, s);
-      s = fmaf(f1.y, qa.w, s);
-      s = fmaf(f2.x, qb.x, s);
-      s = fmaf(f2.y, qb.y, s);
-      s = fmaf(f3.x, qb.z, s);
-      s = fmaf(f3.y, qb.w, s);
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(bits_h2(w[e]));
+        qv[cidx * 8 + 2 * e] = f.x * scale;
+        qv[cidx * 8 + 2 * e + 1] = f.y * scale;
+      }
     }
-    sc[t - p0] = s;
-    lmax = fmaxf(lmax, s);
+  }
+  auto dot = [&](const uint4 (&raw)[CPL]) {
+    float sdot = 0.f;
+#pragma unroll
+    for (int cidx = 0; cidx < CPL; ++cidx) {
+      const uint32_t w[4] = {raw[cidx].x, raw[cidx].y, raw[cidx].z, raw[cidx].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(bits_h2(w[e]));
+        sdot = fmaf(f.x, qv[cidx * 8 + 2 * e], sdot);
+        sdot = fmaf(f.y, qv[cidx * 8 + 2 * e + 1], sdot);
+      }
+    }
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
+    return sdot;
+  };
+  float lmax = -INFINITY;
+  constexpr int kStep = (kAttnThreads / 32) * 8;  // positions per CTA step
+  for (int tb = p0 + warp * 8; tb < p1; tb += 2 * kStep) {  // warp-uniform trip count
+    const int t0 = tb + (lane >> 2), t1 = t0 + kStep;
+    const bool v0 = t0 < p1, v1 = t1 < p1;
+    uint4 r0[CPL], r1[CPL];
+#pragma unroll
+    for (int cidx = 0; cidx < CPL; ++cidx) {
+      r0[cidx] = v0 ? ld_stream16(K + (size_t)t0 * HD + sub * DPL + cidx * 8) : make_uint4(0, 0, 0, 0);
+      r1[cidx] = v1 ? ld_stream16(K + (size_t)t1 * HD + sub * DPL + cidx * 8) : make_uint4(0, 0, 0, 0);
+    }
+    const float s0 = dot(r0), s1 = dot(r1);
+    if (v0) {
+      if (sub == 0) sc[t0 - p0] = s0;
+      lmax = fmaxf(lmax, s0);
+    }
+    if (v1) {
+      if (sub == 0) sc[t1 - p0] = s1;
+      lmax = fmaxf(lmax, s1);
+    }
   }
   const float mx = block_max(lmax, red);
   float lsum = 0.f;
@@ -101,8 +127,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   // pass 2: LPR lanes cover one position row in 16-byte pieces, so a warp load instruction
   // reads RPW whole rows; U such loads per lane are in flight before any is used
   constexpr int LPR = HD / 8, RPW = 32 / LPR, NW = kAttnThreads / 32, STR = NW * RPW, U = 8;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int sub = lane / LPR, ci = lane - sub * LPR;
+  const int vsub = lane / LPR, ci = lane - vsub * LPR;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -118,7 +143,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     acc[6] = fmaf(w, f3.x, acc[6]);
     acc[7] = fmaf(w, f3.y, acc[7]);
   };
-  int t = p0 + warp * RPW + sub;
+  int t = p0 + warp * RPW + vsub;
   for (; t + (U - 1) * STR < p1; t += U * STR) {
     uint4 raw[U];
 #pragma unroll
@@ -131,7 +156,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   for (int o = LPR; o < 32; o <<= 1)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-  if (sub == 0)
+  if (vsub == 0)
 #pragma unroll
     for (int i = 0; i < 8; ++i) accs[warp][ci * 8 + i] = acc[i];
   __syncthreads();
