@@ -149,21 +149,26 @@ constexpr int kTcThreads2 = (kWarpsDq + 3) * 32;
 // 64-k stage, beside the accumulator), which gives a deep A ring without shared memory.
 // Decode tiles (NTILE <= 64) take half of the SM's tensor memory and ~105 KB of shared
 // memory, so two CTAs share an SM; prefill tiles take the whole SM.
-template <int NTILE>
+// OCC: CTAs per SM for decode tiles. 2: 256 TMEM columns each (A ring 6-7 deep), 12-stage
+// weight ring; 3: 128 columns (A ring 2-3 deep), 8-stage weight ring, ~72 KB of shared
+// memory, for grids large enough to put three CTAs on every SM.
+template <int NTILE, int OCC = 2>
 struct TcCfg {
   static constexpr bool kDecode = NTILE <= 64;
-  static constexpr uint32_t kTmemCols = kDecode ? 256 : 512;
+  static constexpr int kMinBlocks = kDecode ? OCC : 1;  // CTAs per SM
+  static constexpr uint32_t kTmemCols = kDecode ? (OCC == 3 ? 128 : 256) : 512;
   static constexpr uint32_t kAccCols = NTILE < 32 ? 32 : NTILE;
   static constexpr int AR = (kTmemCols - kAccCols) / 32 < 8 ? (int)((kTmemCols - kAccCols) / 32) : 8;
-  static constexpr int SW = 12;  // weight ring (<= 12, see below)
-  static constexpr int SX = NTILE <= 32 ? 8 : (NTILE <= 64 ? 6 : (NTILE <= 128 ? 8 : 5));
+  static constexpr int SW = (kDecode && OCC == 3) ? 8 : 12;  // weight ring (<= 12, see below)
+  static constexpr int SX = kDecode ? (OCC == 3 ? (NTILE <= 32 ? 6 : 4) : (NTILE <= 32 ? 8 : 6))
+                                    : (NTILE <= 128 ? 8 : 5);
   static constexpr int XBytes = NTILE * kTcBK * 2;
   static constexpr int OffX = 0;
   static constexpr int OffW = OffX + SX * XBytes;
   static constexpr int OffS = OffW + SW * kWBytes;
   static constexpr int OffBar = OffS + kSRing * kSBytes;
   static constexpr int Bytes = OffBar + 512;
-  static constexpr int kMinBlocks = kDecode ? 2 : 1;
+  static_assert(kMinBlocks * (Bytes + 2048) <= 228 * 1024, "shared memory per SM");
   // A scale slot is refilled 16 stages after its first use; the weight producer only runs
   // SW stages ahead of the dequantisation warps, so SW <= 12 keeps every slot live.
   static_assert(SW <= 12, "scale ring reuse");
@@ -175,11 +180,11 @@ struct TcCfg {
 
 // LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 32 bytes.
 // LAY 1: weights in the tiled layout (qgemm.cuh), read by contiguous bulk copies.
-template <int EPI, int NTILE, int LAY>
-__global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
+template <int EPI, int NTILE, int LAY, int OCC>
+__global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
     tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                     const __grid_constant__ CUtensorMap tms, const QArgs a0) {
-  using C = TcCfg<NTILE>;
+  using C = TcCfg<NTILE, OCC>;
   extern __shared__ __align__(1024) uint8_t smraw[];
   constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NTILE >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 
@@ -428,23 +433,13 @@ bool encode2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
                      sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-size_t tc_smem_bytes(int ntile) {
-  switch (ntile) {
-    case 16: return TcCfg<16>::Bytes + 1024;
-    case 32: return TcCfg<32>::Bytes + 1024;
-    case 64: return TcCfg<64>::Bytes + 1024;
-    case 128: return TcCfg<128>::Bytes + 1024;
-    default: return TcCfg<256>::Bytes + 1024;
-  }
-}
-
-template <int EPI, int NTILE, int LAY>
+template <int EPI, int NTILE, int LAY, int OCC>
 int tc_launch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int KS,
               cudaStream_t st) {
   static bool attr_done[64] = {};
   const int dev = device_index();
-  auto kern = tc_qgemm_kernel<EPI, NTILE, LAY>;
-  const size_t smem = tc_smem_bytes(NTILE);
+  auto kern = tc_qgemm_kernel<EPI, NTILE, LAY, OCC>;
+  const size_t smem = TcCfg<NTILE, OCC>::Bytes + 1024;
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     ORCH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_done[dev] = true;
@@ -466,13 +461,18 @@ void set_tc_min_m(uint32_t m) { g_tc_min_m = m; }
 
 template <int EPI, int LAY>
 int tc_dispatch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int ntile,
-                int KS, cudaStream_t st) {
+                int KS, int occ, cudaStream_t st) {
+  if (occ == 3) switch (ntile) {
+      case 16: return tc_launch<EPI, 16, LAY, 3>(mx, mw, ms, a, KS, st);
+      case 32: return tc_launch<EPI, 32, LAY, 3>(mx, mw, ms, a, KS, st);
+      default: return tc_launch<EPI, 64, LAY, 3>(mx, mw, ms, a, KS, st);
+    }
   switch (ntile) {
-    case 16: return tc_launch<EPI, 16, LAY>(mx, mw, ms, a, KS, st);
-    case 32: return tc_launch<EPI, 32, LAY>(mx, mw, ms, a, KS, st);
-    case 64: return tc_launch<EPI, 64, LAY>(mx, mw, ms, a, KS, st);
-    case 128: return tc_launch<EPI, 128, LAY>(mx, mw, ms, a, KS, st);
-    default: return tc_launch<EPI, 256, LAY>(mx, mw, ms, a, KS, st);
+    case 16: return tc_launch<EPI, 16, LAY, 2>(mx, mw, ms, a, KS, st);
+    case 32: return tc_launch<EPI, 32, LAY, 2>(mx, mw, ms, a, KS, st);
+    case 64: return tc_launch<EPI, 64, LAY, 2>(mx, mw, ms, a, KS, st);
+    case 128: return tc_launch<EPI, 128, LAY, 2>(mx, mw, ms, a, KS, st);
+    default: return tc_launch<EPI, 256, LAY, 2>(mx, mw, ms, a, KS, st);
   }
 }
 
@@ -499,12 +499,26 @@ int tc_qgemm_run(QArgs a, cudaStream_t st) {
   if (tiled) mw = ms = mx;  // unused by the tiled kernel
   const int nblk = (a.K + 4 * kTcBK - 1) / (4 * kTcBK);
   const int tiles = ((a.N + kTcRows - 1) / kTcRows) * ((a.M + ntile - 1) / ntile);
-  const int per_sm = ntile <= 64 ? 2 : 1;  // TcCfg::kMinBlocks
   // split K only as far as one wave of CTAs covers the SMs
-  const int slots = per_sm * num_sms();
-  int KS = 1;
-  while (KS < 8 && tiles * KS * 2 <= slots && nblk >= KS * 4) KS *= 2;
-  const int rc = tiled ? tc_dispatch<EPI, 1>(mx, mw, ms, a, ntile, KS, st) : tc_dispatch<EPI, 0>(mx, mw, ms, a, ntile, KS, st);
+  auto split_for = [&](int per_sm) {
+    const int slots = per_sm * num_sms();
+    int ks = 1;
+    while (ks < 8 && tiles * ks * 2 <= slots && nblk >= ks * 4) ks *= 2;
+    return ks;
+  };
+  // Decode tiles: three CTAs per SM (shallower rings) when the grid is large enough to
+  // fill them, else two (deeper rings); prefill tiles: one.
+  int occ = ntile <= 64 ? 2 : 1;
+  int KS = split_for(occ);
+  if (ntile <= 64) {
+    const int ks3 = split_for(3);
+    if (tiles * ks3 > 2 * num_sms()) {
+      occ = 3;
+      KS = ks3;
+    }
+  }
+  const int rc = tiled ? tc_dispatch<EPI, 1>(mx, mw, ms, a, ntile, KS, occ, st)
+                       : tc_dispatch<EPI, 0>(mx, mw, ms, a, ntile, KS, occ, st);
   if (rc != ORCH_OK) return rc;
   return check_launch("tc_qgemm");
 }
