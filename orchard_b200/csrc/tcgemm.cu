@@ -5,19 +5,19 @@
 // thread per output, weights re-read per row) for the same packed format
 // (orchard/quantizer.py:3-78).
 //
-// D[128 weight rows, NTILE tokens] (fp32, TMEM) += A[128, 16] . B[NTILE, 16]^T per MMA, with
-// four warp roles per CTA:
-//  * a weight producer (one thread) streams packed 128-row x 64-k tiles and their scales
-//    (TMA boxes, or contiguous bulk copies for the tiled layout) into a 12-stage ring,
-//    starting before griddepcontrol.wait;
-//  * an activation producer (one thread) streams the [NTILE, 64] fp16 activation tiles
-//    (TMA, SWIZZLE_128B; rows past M and k past K read as zero) into a shorter ring;
+// D[128 weight rows, NTILE tokens] (fp32, TMEM) += A[128, 16] . B[NTILE, 16]^T per MMA, in
+// stages of 128 k, with four warp roles per CTA:
+//  * a weight producer (one thread) streams packed 128-row x 128-k tiles and their scales
+//    (one 8 KB bulk copy per stage from the tiled layout, or 2-D TMA boxes from the
+//    reference layout) into a 6-stage ring, starting before griddepcontrol.wait;
+//  * an activation producer (one thread) streams the [NTILE, 128] fp16 activation tiles
+//    (two TMA boxes of 64 k, SWIZZLE_128B; rows past M and k past K read as zero);
 //  * eight dequantisation warps turn each packed tile into fp16 (q - 8) * scale with the
 //    magic-exponent trick and store it with tcgen05.st into a ring of A tiles in tensor
-//    memory (6 to 8 stages deep), one weight row per TMEM lane;
-//  * one thread issues tcgen05.mma.kind::f16 with A from tensor memory and B (activations)
-//    from shared memory; tcgen05.commit releases the activation and A slots. Each
-//    handshake is one elected arrival per warp.
+//    memory (3-4 stages deep), one weight row per TMEM lane;
+//  * one thread issues eight tcgen05.mma.kind::f16 per stage with A from tensor memory and
+//    B (activations) from shared memory; tcgen05.commit releases the activation and A
+//    slots. Each handshake is one elected arrival per warp.
 // Decode tiles (NTILE <= 64) use half the tensor memory and ~105 KB of shared memory, so
 // two CTAs share an SM. After the K loop the accumulator is read with tcgen05.ld and handed
 // to the same split-K (cluster / distributed shared memory) reduction and fused epilogues as
@@ -36,7 +36,7 @@
 namespace orch {
 
 constexpr int kTcRows = 128;
-constexpr int kTcBK = 64;  // k per stage: one 128-byte swizzle row of fp16
+constexpr int kTcBK = 128;  // k per stage: two 128-byte swizzle atoms of fp16
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -63,6 +63,18 @@ __device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, ui
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// Thirty-two consecutive 32-bit columns of this thread's TMEM lane; waits for completion.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 // Sixteen consecutive 32-bit columns of this thread's TMEM lane; waits for completion.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -133,8 +145,9 @@ __device__ __forceinline__ uint4 dq8_tiled(uint32_t w, uint32_t sc) {
   return o;
 }
 
-constexpr int kWBytes = kTcRows * (kTcBK / 2);  // packed INT4 tile: 128 rows x 32 bytes
-constexpr int kSBytes = kTcRows * 16;           // scales for 4 stages: 128 rows x 8 fp16
+constexpr int kSub = 64;                           // k per swizzle atom / tiled stage
+constexpr int kWBytes = kTcRows * (kTcBK / 2);     // packed INT4 tile: 128 rows x 64 bytes
+constexpr int kSBytes = kTcRows * 16;              // scales of a 256-k block: 128 rows x 8 fp16
 constexpr int kSRing = 4;
 constexpr int kWarpsDq = 8;                       // dequantisation warps (0-3 also run the epilogue)
 constexpr int kWarpProdW = kWarpsDq;              // TMA producer of weights and scales
@@ -142,49 +155,48 @@ constexpr int kWarpProdX = kWarpsDq + 1;          // TMA producer of activations
 constexpr int kWarpMma = kWarpsDq + 2;            // MMA issuer
 constexpr int kTcThreads2 = (kWarpsDq + 3) * 32;
 
-// Shared-memory and tensor-memory plan. Weights (from HBM) and activations (from L2) have
-// separate shared-memory rings so the weight stream runs far ahead without holding
-// activation tiles: a weight slot is released by the dequantisation warps, an activation
-// slot by the MMA's commit. The dequantised A tiles live in tensor memory (32 columns per
-// 64-k stage, beside the accumulator), which gives a deep A ring without shared memory.
-// Decode tiles (NTILE <= 64) take half of the SM's tensor memory and ~105 KB of shared
-// memory, so two CTAs share an SM; prefill tiles take the whole SM.
-// OCC: CTAs per SM for decode tiles. 2: 256 TMEM columns each (A ring 6-7 deep), 12-stage
-// weight ring; 3: 128 columns (A ring 2-3 deep), 8-stage weight ring, ~72 KB of shared
-// memory, for grids large enough to put three CTAs on every SM.
-template <int NTILE, int OCC = 2>
+// Shared-memory and tensor-memory plan for 128-k stages. Weights (from HBM) and activations
+// (from L2) have separate shared-memory rings so the weight stream runs far ahead without
+// holding activation tiles: a weight slot is released by the dequantisation warps, an
+// activation slot by the MMA's commit. The dequantised A tiles live in tensor memory (64
+// columns per stage, beside the accumulator). Decode tiles (NTILE <= 64) take half of the
+// SM's tensor memory and ~105 KB of shared memory, so two CTAs share an SM; prefill tiles
+// take the whole SM.
+template <int NTILE>
 struct TcCfg {
   static constexpr bool kDecode = NTILE <= 64;
-  static constexpr int kMinBlocks = kDecode ? OCC : 1;  // CTAs per SM
-  static constexpr uint32_t kTmemCols = kDecode ? (OCC == 3 ? 128 : 256) : 512;
+  static constexpr int kMinBlocks = kDecode ? 2 : 1;  // CTAs per SM
+  static constexpr uint32_t kTmemCols = kDecode ? 256 : 512;
   static constexpr uint32_t kAccCols = NTILE < 32 ? 32 : NTILE;
-  static constexpr int AR = (kTmemCols - kAccCols) / 32 < 8 ? (int)((kTmemCols - kAccCols) / 32) : 8;
-  static constexpr int SW = (kDecode && OCC == 3) ? 8 : 12;  // weight ring (<= 12, see below)
-  static constexpr int SX = kDecode ? (OCC == 3 ? (NTILE <= 32 ? 6 : 4) : (NTILE <= 32 ? 8 : 6))
-                                    : (NTILE <= 128 ? 8 : 5);
-  static constexpr int XBytes = NTILE * kTcBK * 2;
+  static constexpr int AR = (kTmemCols - kAccCols) / 64 < 4 ? (int)((kTmemCols - kAccCols) / 64) : 4;
+  static constexpr int SW = 6;  // weight ring (<= 6, see below)
+  static constexpr int SX = NTILE <= 16 ? 6 : (NTILE <= 32 ? 4 : (NTILE <= 128 ? 3 : 2));
+  static constexpr int XSub = NTILE * kSub * 2;  // one 64-k swizzle atom of activations
+  static constexpr int XBytes = 2 * XSub;
   static constexpr int OffX = 0;
   static constexpr int OffW = OffX + SX * XBytes;
   static constexpr int OffS = OffW + SW * kWBytes;
   static constexpr int OffBar = OffS + kSRing * kSBytes;
   static constexpr int Bytes = OffBar + 512;
-  static_assert(kMinBlocks * (Bytes + 2048) <= 228 * 1024, "shared memory per SM");
-  // A scale slot is refilled 16 stages after its first use; the weight producer only runs
-  // SW stages ahead of the dequantisation warps, so SW <= 12 keeps every slot live.
-  static_assert(SW <= 12, "scale ring reuse");
+  // A scale slot serves the two stages of a 256-k block and is refilled 8 stages later; the
+  // weight producer runs at most SW stages ahead of the dequantisation warps, so SW <= 6
+  // keeps every slot live until both of its stages are read.
+  static_assert(SW <= 6, "scale ring reuse");
   static_assert(2 * SW + 2 * SX + 2 * AR + 1 <= 62, "barrier area");
   // the split-K receive buffer reuses the rings and must stay below the barriers
   static_assert((kTcRows + 16) * NTILE * 4 <= OffBar, "receive buffer");
   static_assert(AR >= 2, "A ring");
+  static_assert(kMinBlocks * (Bytes + 2048) <= 228 * 1024, "shared memory per SM");
+  static_assert(XSub % 1024 == 0, "swizzle atoms are 1024-byte aligned");
 };
 
-// LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 32 bytes.
-// LAY 1: weights in the tiled layout (qgemm.cuh), read by contiguous bulk copies.
-template <int EPI, int NTILE, int LAY, int OCC>
-__global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
+// LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 64 bytes.
+// LAY 1: weights in the tiled layout (qgemm.cuh), read by contiguous 8 KB bulk copies.
+template <int EPI, int NTILE, int LAY>
+__global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                     const __grid_constant__ CUtensorMap tms, const QArgs a0) {
-  using C = TcCfg<NTILE, OCC>;
+  using C = TcCfg<NTILE>;
   extern __shared__ __align__(1024) uint8_t smraw[];
   constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NTILE >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 
@@ -206,11 +218,11 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
   const int KS = gridDim.y, ks = blockIdx.y;
   const int R0 = blockIdx.x * kTcRows;
   const int tok0 = blockIdx.z * NTILE;
-  // K is split over the cluster in blocks of 4 stages (one scale tile per block)
-  const int nblk = (a0.K + 4 * kTcBK - 1) / (4 * kTcBK);
-  const int nst_total = LAY == 1 ? 4 * nblk : (a0.K + kTcBK - 1) / kTcBK;
-  const int st0 = ((ks * nblk) / KS) * 4;
-  const int st1 = min(nst_total, (((ks + 1) * nblk) / KS) * 4);
+  // K is split over the cluster in 256-k blocks (two stages, one scale tile)
+  const int nblk = (a0.K + 2 * kTcBK - 1) / (2 * kTcBK);
+  const int nst_total = LAY == 1 ? 2 * nblk : (a0.K + kTcBK - 1) / kTcBK;
+  const int st0 = ((ks * nblk) / KS) * 2;
+  const int st1 = min(nst_total, (((ks + 1) * nblk) / KS) * 2);
   const int nst = st1 - st0;
 
   if (warp == 0) tmem_alloc(tmem_slot, C::kTmemCols);
@@ -237,7 +249,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
-  const uint32_t tmem_a = tmem_d + C::kAccCols;  // A ring: slot i at columns 32 i
+  const uint32_t tmem_a = tmem_d + C::kAccCols;  // A ring: slot i at columns 64 i
 
   bool done_ok = true;
   if (warp == kWarpProdW) {
@@ -252,16 +264,16 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
           *failed = 1;
           break;
         }
-        const bool with_s = (p & 3) == 0;
+        const bool with_s = (p & 1) == 0;
         mbar_expect_tx(&fullW[v], (uint32_t)(kWBytes + (with_s ? kSBytes : 0)));
         if (LAY == 1) {
-          const uint8_t* blk = a0.w + ((size_t)blockIdx.x * nblk + ((st0 + p) >> 2)) * kQ4tBlockBytes;
-          bulk_load(sW + v * kWBytes, blk + ((st0 + p) & 3) * kQ4tStageBytes, kWBytes, &fullW[v]);
-          if (with_s) bulk_load(sS + ((p >> 2) % kSRing) * kSBytes, blk + 4 * kQ4tStageBytes, kSBytes, &fullW[v]);
+          const uint8_t* blk = a0.w + ((size_t)blockIdx.x * nblk + ((st0 + p) >> 1)) * kQ4tBlockBytes;
+          bulk_load(sW + v * kWBytes, blk + ((st0 + p) & 1) * kWBytes, kWBytes, &fullW[v]);
+          if (with_s) bulk_load(sS + ((p >> 1) % kSRing) * kSBytes, blk + 4 * kQ4tStageBytes, kSBytes, &fullW[v]);
         } else {
           const int k0 = (st0 + p) * kTcBK;
           tma_load_2d(sW + v * kWBytes, &tmw, &fullW[v], k0 >> 1, R0);
-          if (with_s) tma_load_2d(sS + ((p >> 2) % kSRing) * kSBytes, &tms, &fullW[v], k0 >> 5, R0);
+          if (with_s) tma_load_2d(sS + ((p >> 1) % kSRing) * kSBytes, &tms, &fullW[v], k0 >> 5, R0);
         }
         issued = p + 1;
       }
@@ -285,7 +297,9 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
           break;
         }
         mbar_expect_tx(&fullX[v], (uint32_t)C::XBytes);
-        tma_load_2d(sX + v * C::XBytes, &tmx, &fullX[v], (st0 + p) * kTcBK, tok0);
+        const int k0 = (st0 + p) * kTcBK;
+        tma_load_2d(sX + v * C::XBytes, &tmx, &fullX[v], k0, tok0);
+        tma_load_2d(sX + v * C::XBytes + C::XSub, &tmx, &fullX[v], k0 + kSub, tok0);
         issued = p + 1;
       }
       if (*failed)
@@ -304,10 +318,12 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
           break;
         }
         tc_fence_after();
-        const uint64_t bd = sw128_desc(smem_u32(sX + v * C::XBytes));
+        const uint64_t bd0 = sw128_desc(smem_u32(sX + v * C::XBytes));
+        const uint64_t bd1 = sw128_desc(smem_u32(sX + v * C::XBytes + C::XSub));
 #pragma unroll
         for (int kk = 0; kk < kTcBK / 16; ++kk)
-          umma_f16_ta(tmem_d, tmem_a + ai * 32 + kk * 8, bd + 2 * kk, kIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ta(tmem_d, tmem_a + ai * 64 + kk * 8, (kk < 4 ? bd0 : bd1) + 2 * (kk & 3), kIdesc,
+                      (s > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&emptyX[v]);
         umma_commit(&aempty[ai]);
       }
@@ -316,10 +332,10 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
     __syncwarp();
   } else {
     // ------- dequantisation warps: packed tile -> fp16 A tile in tensor memory -------
-    // Warp w owns TMEM lanes 32 (w % 4) .. + 31 (= weight rows); warps 0-3 write k 0..31 of
-    // each stage (columns 0..15 of the slot), warps 4-7 k 32..63 (columns 16..31).
+    // Warp w owns TMEM lanes 32 (w % 4) .. + 31 (= weight rows); warps 0-3 write k 0..63 of
+    // each stage (columns 0..31 of the slot), warps 4-7 k 64..127 (columns 32..63).
     pdl_wait();
-    const int h = warp >> 2, r = (warp & 3) * 32 + lane;
+    const int j2 = warp >> 2, r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     for (int s = 0; s < nst; ++s) {
       const int v = s % C::SW, ai = s % C::AR;
@@ -330,29 +346,35 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE, OCC>::kMinBlocks)
         break;
       }
       const uint8_t* wt = sW + v * kWBytes;
-      const __half* st = reinterpret_cast<const __half*>(sS + ((s >> 2) % kSRing) * kSBytes);
-      uint4 w4;
-      uint32_t sc;
-      if (LAY == 1) {  // [2 halves][128 rows][16 B], scales [8 groups][128 rows]
-        w4 = *reinterpret_cast<const uint4*>(wt + h * (kWBytes / 2) + r * 16);
-        sc = h2_bits(__half2half2(st[((s & 3) * 2 + h) * kTcRows + r]));
-      } else {  // TMA boxes: [128 rows][32 B], scales [128 rows][8 groups]
-        w4 = *reinterpret_cast<const uint4*>(wt + r * 32 + h * 16);
-        sc = h2_bits(__half2half2(st[r * 8 + (s & 3) * 2 + h]));
+      const __half* st = reinterpret_cast<const __half*>(sS + ((s >> 1) % kSRing) * kSBytes);
+      const int g0 = ((s & 1) * 2 + j2) * 2;  // scale group of this warp's first 32 k in the block
+      uint4 wa, wb;
+      uint32_t sca, scb;
+      if (LAY == 1) {  // 64-k stages [2 halves][128 rows][16 B]; scales [8 groups][128 rows]
+        wa = *reinterpret_cast<const uint4*>(wt + j2 * kQ4tStageBytes + r * 16);
+        wb = *reinterpret_cast<const uint4*>(wt + j2 * kQ4tStageBytes + (kQ4tStageBytes / 2) + r * 16);
+        sca = h2_bits(__half2half2(st[g0 * kTcRows + r]));
+        scb = h2_bits(__half2half2(st[(g0 + 1) * kTcRows + r]));
+      } else {  // TMA boxes: [128 rows][64 B], scales [128 rows][8 groups]
+        wa = *reinterpret_cast<const uint4*>(wt + r * 64 + j2 * 32);
+        wb = *reinterpret_cast<const uint4*>(wt + r * 64 + j2 * 32 + 16);
+        sca = h2_bits(__half2half2(st[r * 8 + g0]));
+        scb = h2_bits(__half2half2(st[r * 8 + g0 + 1]));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
-      const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
-      uint32_t q[16];
+      const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      uint32_t q[32];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t sc = i < 4 ? sca : scb;
         const uint4 o = LAY == 1 ? dq8_tiled(wv[i], sc) : dq8_natural(wv[i], sc);
         q[4 * i] = o.x;
         q[4 * i + 1] = o.y;
         q[4 * i + 2] = o.z;
         q[4 * i + 3] = o.w;
       }
-      tmem_st16(tmem_a + lane_base + ai * 32 + h * 16, q);
+      tmem_st32(tmem_a + lane_base + ai * 64 + j2 * 32, q);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[ai]);
@@ -433,13 +455,13 @@ bool encode2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
                      sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI, int NTILE, int LAY, int OCC>
+template <int EPI, int NTILE, int LAY>
 int tc_launch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int KS,
               cudaStream_t st) {
   static bool attr_done[64] = {};
   const int dev = device_index();
-  auto kern = tc_qgemm_kernel<EPI, NTILE, LAY, OCC>;
-  const size_t smem = TcCfg<NTILE, OCC>::Bytes + 1024;
+  auto kern = tc_qgemm_kernel<EPI, NTILE, LAY>;
+  const size_t smem = TcCfg<NTILE>::Bytes + 1024;
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     ORCH_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_done[dev] = true;
@@ -461,18 +483,13 @@ void set_tc_min_m(uint32_t m) { g_tc_min_m = m; }
 
 template <int EPI, int LAY>
 int tc_dispatch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int ntile,
-                int KS, int occ, cudaStream_t st) {
-  if (occ == 3) switch (ntile) {
-      case 16: return tc_launch<EPI, 16, LAY, 3>(mx, mw, ms, a, KS, st);
-      case 32: return tc_launch<EPI, 32, LAY, 3>(mx, mw, ms, a, KS, st);
-      default: return tc_launch<EPI, 64, LAY, 3>(mx, mw, ms, a, KS, st);
-    }
+                int KS, cudaStream_t st) {
   switch (ntile) {
-    case 16: return tc_launch<EPI, 16, LAY, 2>(mx, mw, ms, a, KS, st);
-    case 32: return tc_launch<EPI, 32, LAY, 2>(mx, mw, ms, a, KS, st);
-    case 64: return tc_launch<EPI, 64, LAY, 2>(mx, mw, ms, a, KS, st);
-    case 128: return tc_launch<EPI, 128, LAY, 2>(mx, mw, ms, a, KS, st);
-    default: return tc_launch<EPI, 256, LAY, 2>(mx, mw, ms, a, KS, st);
+    case 16: return tc_launch<EPI, 16, LAY>(mx, mw, ms, a, KS, st);
+    case 32: return tc_launch<EPI, 32, LAY>(mx, mw, ms, a, KS, st);
+    case 64: return tc_launch<EPI, 64, LAY>(mx, mw, ms, a, KS, st);
+    case 128: return tc_launch<EPI, 128, LAY>(mx, mw, ms, a, KS, st);
+    default: return tc_launch<EPI, 256, LAY>(mx, mw, ms, a, KS, st);
   }
 }
 
@@ -489,7 +506,7 @@ int tc_qgemm_run(QArgs a, cudaStream_t st) {
   const int ntile = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
   CUtensorMap mx, mw, ms;
   bool ok = encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,
-                     kTcBK, ntile, CU_TENSOR_MAP_SWIZZLE_128B);
+                     kSub, ntile, CU_TENSOR_MAP_SWIZZLE_128B);
   if (ok && !tiled)
     ok = encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N, (uint64_t)(a.K / 2),
                   kTcBK / 2, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
@@ -497,28 +514,14 @@ int tc_qgemm_run(QArgs a, cudaStream_t st) {
                   (uint64_t)(a.K / 32) * 2, 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!ok) return fail(ORCH_ERR_UNSUPPORTED, "tensor map encode failed");
   if (tiled) mw = ms = mx;  // unused by the tiled kernel
-  const int nblk = (a.K + 4 * kTcBK - 1) / (4 * kTcBK);
+  const int nblk = (a.K + 2 * kTcBK - 1) / (2 * kTcBK);  // 256-k blocks
   const int tiles = ((a.N + kTcRows - 1) / kTcRows) * ((a.M + ntile - 1) / ntile);
   // split K only as far as one wave of CTAs covers the SMs
-  auto split_for = [&](int per_sm) {
-    const int slots = per_sm * num_sms();
-    int ks = 1;
-    while (ks < 8 && tiles * ks * 2 <= slots && nblk >= ks * 4) ks *= 2;
-    return ks;
-  };
-  // Decode tiles: three CTAs per SM (shallower rings) when the grid is large enough to
-  // fill them, else two (deeper rings); prefill tiles: one.
-  int occ = ntile <= 64 ? 2 : 1;
-  int KS = split_for(occ);
-  if (ntile <= 64) {
-    const int ks3 = split_for(3);
-    if (tiles * ks3 > 2 * num_sms()) {
-      occ = 3;
-      KS = ks3;
-    }
-  }
-  const int rc = tiled ? tc_dispatch<EPI, 1>(mx, mw, ms, a, ntile, KS, occ, st)
-                       : tc_dispatch<EPI, 0>(mx, mw, ms, a, ntile, KS, occ, st);
+  const int slots = (ntile <= 64 ? 2 : 1) * num_sms();  // TcCfg::kMinBlocks
+  int KS = 1;
+  while (KS < 8 && tiles * KS * 2 <= slots && nblk >= KS * 4) KS *= 2;
+  const int rc = tiled ? tc_dispatch<EPI, 1>(mx, mw, ms, a, ntile, KS, st)
+                       : tc_dispatch<EPI, 0>(mx, mw, ms, a, ntile, KS, st);
   if (rc != ORCH_OK) return rc;
   return check_launch("tc_qgemm");
 }
