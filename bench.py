@@ -344,6 +344,19 @@ def cpu_baseline_sample(B, target_s=15.0):
             "step_s": step_s}
 
 
+# DRAM bytes (read + write) per decode step of each kernel family at batch 64, from one ncu
+# capture of a 2-layer model of these shapes scaled to the layer count (the capture, its
+# command and the per-launch figures are summarised in profiles/decode_b64_traffic.md).
+_TRAFFIC_B64 = {"qgemm": {"per_layer": 28.88e6 + 2 * 19.45e6 + 51.29e6, "once": 74.46e6}}
+
+
+def _traffic(family, layers, batch):
+    t = _TRAFFIC_B64.get(family)
+    if t is None or batch != 64:
+        return None
+    return round(t["per_layer"] * layers + t["once"])
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -402,7 +415,7 @@ def run_ours(args):
     prof_ms = sum(v["ms"] for v in prof.values())
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": "measured" if peaks else "fallback",
-                "traffic": None, "launches_per_step": d["launches"],
+                "traffic": _traffic(dom, args.layers, B), "launches_per_step": d["launches"],
                 "bytes_per_step": d["bytes"], "share_of_eager_step": round(d["ms"] / prof_ms, 3),
                 "families_ms": {k: round(v["ms"], 4) for k, v in prof.items()}}
     step_bytes = sum(v["bytes"] for v in prof.values())
