@@ -211,6 +211,13 @@ int orch_argmax_pairs(const float* logits, uint32_t M, uint32_t V, uint32_t base
                       void* stream);
 int orch_argmax_merge(const float* pairs, uint32_t world, uint32_t B, uint32_t row0, uint32_t rows,
                       int32_t* tok, void* stream);
+/* Temperature sampling on the device, replacing the host sampler of orchard/model.py:244-252:
+ * per row of logits [M, V] (fp32), p = softmax((l - max) / T) in fp32, and the token is the
+ * first id whose running sum of p exceeds uniforms[row] (the inverse CDF that
+ * np.random.choice evaluates with its one uniform draw; the caller draws the uniforms from
+ * its own RNG, so the NumPy stream of the reference can be followed). */
+int orch_sample_rows(const float* logits, uint32_t M, uint32_t V, float temperature,
+                     const float* uniforms, int32_t* tok, void* stream);
 /* Decode attention that allocates nothing (no counterpart in the reference). Same inputs,
  * outputs and arithmetic as orch_attention_decode, but the split-position partials live in
  * a 1 MiB array inside the library (orch_attention_noalloc_max_bytes()) that every GPU

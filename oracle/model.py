@@ -132,6 +132,14 @@ class OracleModel:
         """``generate_batch(..., temperature=0)`` token flow (orchard/model.py:254-381):
         token-by-token prefill per sequence, the last prompt token fed again as the first
         decode input at position ``len(prompt)``, greedy argmax, EOS id 2 retires a row."""
+        return self.generate(prompts, max_tokens, 0.0, ignore_eos)
+
+    def generate(self, prompts: List[List[int]], max_tokens: int, temperature: float,
+                 ignore_eos: bool = False) -> List[List[int]]:
+        """``generate_batch`` token flow (orchard/model.py:254-381) with its sampler
+        (orchard/model.py:244-252): argmax at temperature 0, otherwise
+        ``np.random.choice`` over ``softmax((logits - max) / T)`` in float32, one call per
+        active row in row order (so the draws follow the global NumPy RNG stream)."""
         self.reset()
         cur = []
         for b, ids in enumerate(prompts):
@@ -148,13 +156,23 @@ class OracleModel:
             lg = self.forward_tokens(toks, pos, active)
             nxt = []
             for i, b in enumerate(active):
-                t = int(np.argmax(lg[i]))
+                t = int(np.argmax(lg[i])) if temperature == 0 else sample(lg[i], temperature)
                 gen[b].append(t)
                 cur[b] = t
                 if ignore_eos or t != EOS_ID:
                     nxt.append(b)
             active = nxt
         return gen
+
+
+def sample(logits: np.ndarray, temperature: float) -> int:
+    """orchard/model.py:247-252: shift by the max, float32 softmax of logits / T, then
+    ``np.random.choice`` (one uniform from the global RNG; the first index whose normalised
+    running sum exceeds it)."""
+    lg = np.asarray(logits, np.float32)
+    lg = lg - np.max(lg)
+    probs = np.exp(lg / temperature) / np.sum(np.exp(lg / temperature))
+    return int(np.random.choice(len(probs), p=probs))
 
 
 def random_model(config: dict, seed: int = 0, lora_rank: int = 0,

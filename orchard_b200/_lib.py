@@ -86,6 +86,7 @@ _SIGS = {
     "orch_set_tc_min_m": (_i32, [_u32]),
     "orch_argmax_pairs": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "orch_argmax_merge": (_i32, [_vp, _u32, _u32, _u32, _u32, _vp, _vp]),
+    "orch_sample_rows": (_i32, [_vp, _u32, _u32, C.c_float, _vp, _vp, _vp]),
     "orch_attention_noalloc_max_bytes": (_sz, []),
     "orch_attention_decode_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
     "orch_argmax_rows": (_i32, [_vp, _u32, _u32, _vp, _vp]),

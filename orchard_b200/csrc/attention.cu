@@ -382,6 +382,68 @@ extern "C" int orch_argmax_pairs(const float* logits, uint32_t M, uint32_t V, ui
 }
 
 namespace orch {
+// Temperature sampling of one row per CTA (orchard/model.py:247-252 with np.random.choice):
+// e_i = exp((l_i - max) / T) in fp32, then the first index whose running sum exceeds
+// u * sum(e) for the row's uniform u (the inverse CDF np.random.choice evaluates). Each
+// thread owns a contiguous chunk; chunk sums are scanned across the block, and the thread
+// whose chunk holds the crossing walks it in order.
+__global__ void __launch_bounds__(1024) sample_rows_kernel(const float* logits, int V, float temperature,
+                                                           const float* uniforms, int* tok) {
+  __shared__ float red[32];
+  __shared__ float wsum[32];
+  __shared__ int found;
+  pdl_trigger();
+  pdl_wait();
+  const float* r = logits + (size_t)blockIdx.x * V;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, r[i]);
+  mx = block_max(mx, red);
+  const int chunk = (V + blockDim.x - 1) / blockDim.x;
+  const int c0 = min(V, (int)threadIdx.x * chunk), c1 = min(V, c0 + chunk);
+  float local = 0.f;
+  for (int i = c0; i < c1; ++i) local += expf((r[i] - mx) / temperature);
+  // inclusive scan of the chunk sums over the block
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wsum[w] = incl;
+  if (threadIdx.x == 0) found = 0;
+  __syncthreads();
+  float wprefix = 0.f, total = 0.f;
+  for (int j = 0; j < (int)(blockDim.x >> 5); ++j) {
+    if (j < w) wprefix += wsum[j];
+    total += wsum[j];
+  }
+  const float before = wprefix + incl - local;  // sum of all earlier chunks
+  const float target = uniforms[blockIdx.x] * total;
+  if (local > 0.f && before <= target && target < before + local) {
+    float run = before;
+    int pick = c1 - 1;
+    for (int i = c0; i < c1; ++i) {
+      run += expf((r[i] - mx) / temperature);
+      if (run > target) {
+        pick = i;
+        break;
+      }
+    }
+    if (atomicCAS(&found, 0, 1) == 0) tok[blockIdx.x] = pick;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !found) {  // rounding put the target past the last sum: the argmax
+    int best = 0;
+    for (int i = 0; i < V; ++i)
+      if (r[i] == mx) {
+        best = i;
+        break;
+      }
+    tok[blockIdx.x] = best;
+  }
+}
+
 // One thread per row: the highest value over the ranks' pairs, the lowest id among equal
 // values, a NaN wins (np.argmax over the whole vocabulary).
 __global__ void argmax_merge_kernel(const float2* pairs, int world, int B, int row0, int rows, int* tok) {
@@ -398,6 +460,16 @@ __global__ void argmax_merge_kernel(const float2* pairs, int world, int B, int r
   tok[r] = (int)best.y;
 }
 }  // namespace orch
+
+extern "C" int orch_sample_rows(const float* logits, uint32_t M, uint32_t V, float temperature,
+                                const float* uniforms, int32_t* tok, void* stream) {
+  if (M == 0) return ORCH_OK;
+  ORCH_REQUIRE(logits && uniforms && tok && V > 0, "sample_rows: bad arguments");
+  ORCH_REQUIRE(temperature > 0.f, "sample_rows: temperature must be positive (0 is argmax)");
+  ORCH_CUDA(launch_k(sample_rows_kernel, dim3(M), dim3(1024), 0, as_stream(stream), dim3(0, 0, 0), logits, (int)V,
+                     temperature, uniforms, (int*)tok));
+  return check_launch("sample_rows");
+}
 
 // Merge the all-gathered pairs [world][B][2] for rows row0 .. row0 + rows - 1 into tokens.
 extern "C" int orch_argmax_merge(const float* pairs, uint32_t world, uint32_t B, uint32_t row0, uint32_t rows,

@@ -221,6 +221,7 @@ class RowBuffers:
         self.tok_out = torch.zeros(rows, dtype=torch.int32, device=device)
         self.pos = torch.zeros(rows, dtype=torch.int32, device=device)
         self.slots = torch.arange(rows, dtype=torch.int32, device=device)
+        self.uniforms = torch.full((rows,), 0.5, dtype=torch.float32, device=device)  # sampler draws
         self.lora_t = torch.zeros((rows, 3 * 64), dtype=torch.float32, device=device)
         lib = _lib.lib()
         ms = list(range(1, min(rows, 256) + 1)) + [rows]  # splits only happen for few rows
@@ -442,8 +443,10 @@ class DecodeEngine:
             else:
                 call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
 
-    def run_head(self, M: int):
-        """Final RMSNorm, INT4 lm_head (fp32 logits) and argmax into tok_out."""
+    def run_head(self, M: int, temperature: float = 0.0):
+        """Final RMSNorm, INT4 lm_head (fp32 logits) and the next token into tok_out: the
+        argmax, or for temperature > 0 a draw from softmax(logits / T) with the row's
+        uniform in ``uniforms`` (orchard/model.py:244-252)."""
         b = self.dec
         cfg, s = self.cfg, _stream()
         H, V = cfg.hidden_size, cfg.vocab_size
@@ -456,7 +459,10 @@ class DecodeEngine:
         else:
             call("orch_gemm_q4_0_ex", ptr(self.lm_w), ptr(self.lm_s), ptr(b.xn), F16, ptr(b.logits), F32,
                  H, V, M, s)
-        call("orch_argmax_rows", ptr(b.logits), M, V, ptr(b.tok_out), s)
+        if temperature > 0:
+            call("orch_sample_rows", ptr(b.logits), M, V, float(temperature), ptr(b.uniforms), ptr(b.tok_out), s)
+        else:
+            call("orch_argmax_rows", ptr(b.logits), M, V, ptr(b.tok_out), s)
 
     def prefill_rows(self, tokens: np.ndarray, positions: np.ndarray, slots: np.ndarray, chunk: int = 4096):
         """Batched prefill: every prompt token is a row with its own position and cache slot,
@@ -507,14 +513,17 @@ class DecodeEngine:
             n += len(self.layers)
         return n + ((4 if self.split is not None else 3) if logits else 0)
 
-    def step(self, M: int, logits: bool = True, graph: bool = True):
+    def step(self, M: int, logits: bool = True, graph: bool = True, temperature: float = 0.0):
         """One decode (or prefill) step for rows [0, M); with `graph` the step is replayed
-        from a captured CUDA graph."""
-        key = (M, logits)
+        from a captured CUDA graph. ``temperature`` > 0 samples with the uniforms in
+        ``self.dec.uniforms`` instead of taking the argmax."""
+        if temperature > 0 and self.split is not None:
+            raise ValueError("the column split samples greedily")
+        key = (M, logits, float(temperature))
         if not graph:
             self.run_layers(M)
             if logits:
-                self.run_head(M)
+                self.run_head(M, temperature)
             return
         g = self.graphs.get(key)
         if g is None:
@@ -524,14 +533,14 @@ class DecodeEngine:
             with torch.cuda.stream(side):
                 self.run_layers(M)
                 if logits:
-                    self.run_head(M)
+                    self.run_head(M, temperature)
             torch.cuda.current_stream().wait_stream(side)
             torch.cuda.synchronize(self.device)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 self.run_layers(M)
                 if logits:
-                    self.run_head(M)
+                    self.run_head(M, temperature)
             self.graphs[key] = g
             # capture only records; the step itself still has to run
         g.replay()
@@ -622,7 +631,10 @@ class Llama:
         tokens device->host. With temperature 0 the next step is enqueued before the host
         reads the previous step's tokens, so the GPU never waits on the host; a row that
         produced EOS keeps computing (its later tokens are dropped), which leaves the other
-        rows' results unchanged. ``stats`` (optional dict) receives the prefill and decode
+        rows' results unchanged. With temperature > 0 the softmax and the draw run on the
+        device too: the host draws one uniform per active row from the global NumPy RNG, in
+        row order (the draws np.random.choice makes in the reference), and copies them in
+        with the positions. ``stats`` (optional dict) receives the prefill and decode
         wall times, steps run and bytes copied per step."""
         import time
 
@@ -643,6 +655,7 @@ class Llama:
         pos_host = torch.empty((max_tokens, B), dtype=torch.int32, pin_memory=True)
         pos_host.copy_(torch.as_tensor(lens[None, :] + np.arange(max_tokens, dtype=np.int32)[:, None]))
         tok_host = torch.empty((max_tokens, B), dtype=torch.int32, pin_memory=True)
+        u_host = torch.empty((max_tokens, B), dtype=torch.float32, pin_memory=True)
         gen: List[List[int]] = [[] for _ in range(B)]
         active = np.ones(B, dtype=bool)
         greedy = temperature == 0
@@ -664,7 +677,13 @@ class Llama:
             if not active.any() and eng.split is None:  # split ranks stay in step together
                 break
             eng.pos[:B].copy_(pos_host[step], non_blocking=True)
-            eng.step(B, logits=True, graph=self.use_graphs)
+            if not greedy:  # one uniform per active row, in row order (the reference's draws)
+                u = np.full(B, 0.5, np.float32)
+                act = np.nonzero(active)[0]
+                u[act] = np.random.random_sample(len(act))
+                u_host[step].copy_(torch.as_tensor(u))
+                eng.dec.uniforms[:B].copy_(u_host[step], non_blocking=True)
+            eng.step(B, logits=True, graph=self.use_graphs, temperature=temperature)
             if greedy:
                 eng.tok_in[:B].copy_(eng.tok_out[:B])
                 tok_host[step].copy_(eng.tok_out[:B], non_blocking=True)
@@ -672,13 +691,16 @@ class Llama:
                 ev.record(stream)
                 events.append(ev)
             else:
-                lg = eng.logits[:B].cpu().numpy()
-                nxt = np.array([self._sample(lg[b], temperature) if active[b] else 0 for b in range(B)], np.int32)
+                tok_host[step].copy_(eng.tok_out[:B], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                ev.synchronize()
+                nxt = tok_host[step].numpy()
                 for b in np.nonzero(active)[0]:
                     gen[b].append(int(nxt[b]))
                     if not ignore_eos and nxt[b] == EOS_ID:
                         active[b] = False
-                eng.tok_in[:B].copy_(torch.as_tensor(nxt).to(eng.device))
+                eng.tok_in[:B].copy_(eng.tok_out[:B])
             steps += 1
         if greedy and steps > 0 and len(events) == steps and active.any():
             consume(steps - 1)
@@ -686,5 +708,5 @@ class Llama:
         t2 = time.perf_counter()
         if stats is not None:
             stats.update(prefill_s=t1 - t0, decode_s=t2 - t1, steps=steps, batch=B,
-                         h2d_bytes_per_step=4 * B, d2h_bytes_per_step=4 * B if greedy else 4 * B * eng.cfg.vocab_size)
+                         h2d_bytes_per_step=4 * B if greedy else 8 * B, d2h_bytes_per_step=4 * B)
         return gen

@@ -31,6 +31,9 @@ def golden_model():
         "tokens": [[int(v) for v in r if v >= 0] for r in d["tokens"]],
         "tokens_lora": [[int(v) for v in r if v >= 0] for r in d["tokens_lora"]],
         "logits": d["logits"], "logits_lora": d["logits_lora"],
+        "tokens_sampled": [[int(v) for v in r if v >= 0] for r in d["tokens_sampled"]],
+        "sample_t": float(d["sample_t_seed_tokens"][0]), "sample_seed": int(d["sample_t_seed_tokens"][1]),
+        "sample_tokens": int(d["sample_t_seed_tokens"][2]),
     }
 
 

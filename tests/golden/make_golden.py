@@ -12,7 +12,8 @@ committed so the tests never need the reference at run time.
   quantises with the reference quantizer) and run through the reference
   ``Llama.generate_batch`` (orchard/model.py:254-381) at temperature 0, with and
   without a rank-4 LoRA adapter (orchard/loader.py:150-254). Logits of every
-  decode step are captured from ``Llama._sample``.
+  decode step are captured from ``Llama._sample``. A third run samples at temperature
+  0.7 from ``np.random.seed(20261201)`` (``Llama._sample``'s ``np.random.choice``).
 * ``layer_trace.npz``    -- ``LlamaLayer.forward`` (orchard/model.py:78-195) called
   token by token on one sequence, then on a batch of two sequences at different
   positions.
@@ -47,6 +48,7 @@ CONFIG = {
 }
 PROMPTS = [[5, 17, 33, 8, 61], [12, 40, 3, 29, 50, 7, 44]]
 MAX_TOKENS = 6
+SAMPLE_T, SAMPLE_SEED, SAMPLE_TOKENS = 0.7, 20261201, 16  # sampled run (np.random.choice)
 LORA_R, LORA_ALPHA = 4, 8
 
 
@@ -153,7 +155,7 @@ class IdTokenizer:
         return " ".join(str(int(v)) for v in ids)
 
 
-def run_generate(orchard, model_dir, adapter_dir=None):
+def run_generate(orchard, model_dir, adapter_dir=None, temperature=0.0, max_tokens=MAX_TOKENS, seed=None):
     llama = orchard.model.Llama(model_dir)
     if adapter_dir:
         llama.load_lora(adapter_dir)
@@ -166,8 +168,10 @@ def run_generate(orchard, model_dir, adapter_dir=None):
         return orig(lg, temperature)
 
     llama._sample = rec
+    if seed is not None:
+        np.random.seed(seed)
     texts = llama.generate_batch([" ".join(map(str, p)) for p in PROMPTS],
-                                 max_tokens=MAX_TOKENS, temperature=0)
+                                 max_tokens=max_tokens, temperature=temperature)
     toks = [[int(v) for v in s.split()] for s in texts]
     return llama, toks, logits
 
@@ -222,6 +226,7 @@ def main():
         llama, toks, logits = run_generate(orchard, mdir)
         trace = layer_trace(orchard, llama)
         _, toks_l, logits_l = run_generate(orchard, mdir, adir)
+        _, toks_s, _ = run_generate(orchard, mdir, temperature=SAMPLE_T, max_tokens=SAMPLE_TOKENS, seed=SAMPLE_SEED)
 
     pad = max(len(t) for t in toks + toks_l)
     out = {f"ckpt/{k}": v for k, v in ckpt.items()}
@@ -234,6 +239,9 @@ def main():
     out["tokens_lora"] = np.array([t + [-1] * (pad - len(t)) for t in toks_l])
     out["logits"] = np.stack(logits)
     out["logits_lora"] = np.stack(logits_l)
+    pad_s = max(len(t) for t in toks_s)
+    out["tokens_sampled"] = np.array([t + [-1] * (pad_s - len(t)) for t in toks_s])
+    out["sample_t_seed_tokens"] = np.array([SAMPLE_T, SAMPLE_SEED, SAMPLE_TOKENS])
     np.savez_compressed(os.path.join(HERE, "tiny_model.npz"), **out)
     np.savez_compressed(os.path.join(HERE, "layer_trace.npz"), **trace)
     print("tokens", toks, "tokens_lora", toks_l)

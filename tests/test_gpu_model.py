@@ -53,6 +53,50 @@ def test_generate_matches_reference_golden(golden_model, graphs, tiled):
         assert rel_err(lgs[s], ref[s]) <= 1e-2
 
 
+@pytest.mark.parametrize("graphs", [True, False])
+def test_sampled_generate_matches_reference_golden(golden_model, graphs):
+    """temperature 0.7 from the seeded global NumPy RNG: softmax and draw on the device
+    (one host uniform per active row), the reference's tokens, including the row that samples
+    EOS and retires."""
+    g = golden_model
+    llm = Llama.from_tensors(g["config"], g["ckpt"], max_batch=4, use_graphs=graphs)
+    np.random.seed(g["sample_seed"])
+    toks = llm.generate_batch_ids(g["prompts"], max_tokens=g["sample_tokens"], temperature=g["sample_t"])
+    assert toks == g["tokens_sampled"]
+
+
+def test_sample_rows_kernel_inverse_cdf():
+    """orch_sample_rows against np.random.choice's inverse CDF (searchsorted of the
+    normalised float32 running sum, side='right') on random logits; uniforms are kept away
+    from the CDF steps by more than the float32 rounding of the sums."""
+    from orchard_b200._lib import call
+    g = np.random.default_rng(5)
+    M, V = 40, 32000
+    logits = (g.standard_normal((M, V)) * 3).astype(np.float32)
+    logits[7, 1234] = 40.0  # one row with a dominant token
+    T = 0.7
+    u = np.empty(M, np.float32)
+    want = np.empty(M, np.int64)
+    for r in range(M):
+        lg = logits[r] - logits[r].max()
+        p = np.exp(lg / T) / np.sum(np.exp(lg / T))
+        cdf = np.cumsum(p.astype(np.float64))
+        cdf /= cdf[-1]
+        while True:
+            x = np.float32(g.random())
+            i = int(np.searchsorted(cdf, x, side="right"))
+            lo = cdf[i - 1] if i > 0 else 0.0
+            if min(x - lo, cdf[i] - x) > 1e-5:
+                break
+        u[r], want[r] = x, i
+    tok = torch.empty(M, dtype=torch.int32, device="cuda")
+    call("orch_sample_rows", torch.from_numpy(logits).cuda(), M, V, T, torch.from_numpy(u).cuda(), tok,
+         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(tok.cpu().numpy(), want)
+    assert tok[7].item() == 1234
+
+
 def test_generate_with_lora_matches_reference_golden(golden_model, tmp_path):
     from safetensors.numpy import save_file
     g = golden_model

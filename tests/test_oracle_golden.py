@@ -88,6 +88,17 @@ def test_oracle_generate_matches_reference(golden_model, with_lora):
     np.testing.assert_allclose(np.array(seen), ref, atol=1e-5, rtol=1e-5)
 
 
+def test_oracle_sampled_generate_matches_reference(golden_model):
+    """temperature 0.7 from a seeded global NumPy RNG: the reference's tokens, including a
+    row that samples EOS and retires (so later draws skip it)."""
+    g = golden_model
+    m = oracle.model.from_hf_tensors(g["config"], g["ckpt"])
+    np.random.seed(g["sample_seed"])
+    toks = m.generate(g["prompts"], g["sample_tokens"], g["sample_t"])
+    assert toks == g["tokens_sampled"]
+    assert any(t[-1] == 2 for t in toks)
+
+
 def test_oracle_layer_trace(golden_model, golden_trace):
     g = golden_model
     m = oracle.model.from_hf_tensors(g["config"], g["ckpt"])
