@@ -191,3 +191,33 @@ def test_seven_b_two_layer_slice_matches_oracle():
         for b in range(2):
             if top2[b, 1] - top2[b, 0] > 1e-2 * np.abs(ref[b]).max():
                 assert toks[b, s] == int(np.argmax(ref[b]))
+
+
+def test_optimize_then_load_matches_reference(golden_model, tmp_path):
+    """The pre-quantised checkpoint path end to end: optimizer.optimize_model writes the
+    reference's packed format (bit-identical to the reference packer, via the host packer
+    that the golden fixtures pin), and Llama loads it and reproduces the reference tokens."""
+    from safetensors.numpy import load_file, save_file
+
+    from orchard_b200 import quantizer
+    from orchard_b200.optimizer import optimize_model
+    g = golden_model
+    src, dst = tmp_path / "hf", tmp_path / "packed"
+    src.mkdir()
+    save_file(g["ckpt"], str(src / "model.safetensors"))
+    (src / "config.json").write_text(json.dumps(g["config"]))
+    optimize_model(str(src), str(dst))
+    out = load_file(str(dst / "model.safetensors"))
+    n_packed = 0
+    for key, w in g["ckpt"].items():
+        if ("model.layers" in key and "norm" not in key) or key == "lm_head.weight":
+            p, s = quantizer.quantize_q4_0(w.astype(np.float32))
+            assert np.array_equal(out[key.replace(".weight", ".weight_packed")], p)
+            assert np.array_equal(out[key.replace(".weight", ".weight_scales")].view(np.uint16), s.view(np.uint16))
+            n_packed += 1
+        else:
+            assert np.array_equal(out[key], w)
+    assert n_packed == 2 * 7 + 1
+    assert json.loads((dst / "config.json").read_text()) == g["config"]
+    llm = Llama(str(dst), max_batch=4)
+    assert llm.generate_batch_ids(g["prompts"], max_tokens=g["max_tokens"], temperature=0) == g["tokens"]
