@@ -56,6 +56,7 @@ static int ensure_device_state(int d) {
     ORCH_CUDA(cudaMalloc(&p, 256));
     ORCH_CUDA(cudaMemset(p, 0, 256));
     g_check[d] = static_cast<uint32_t*>(p);
+    sk_preallocate(d, g_sms[d]);
   }
   return ORCH_OK;
 }

@@ -62,6 +62,12 @@ int qgemm_run(QArgs a, cudaStream_t st);
 // shape is outside what it implements.
 template <int EPI>
 int tc_qgemm_run(QArgs a, cudaStream_t st);
+// Persistent stream-K tensor-core path for tiled INT4 weights and M <= 64 (tcgemm_sk.cu);
+// ORCH_ERR_UNSUPPORTED when it does not apply.
+template <int EPI>
+int tc_sk_run(QArgs a, cudaStream_t st);
+// Allocates device `dev`'s pool of stream-K workspaces (called once per device).
+void sk_preallocate(int dev, int sms);
 // Activation-row count from which INT4 GEMMs take the tensor-core path (0 = never).
 uint32_t tc_min_m();
 // mma.sync GEMV on tiled weights for M <= gemv_max_m() (gemv.cu).
@@ -135,17 +141,27 @@ __device__ __forceinline__ float* epi_dest(cg::cluster_group& cl, float* recv, i
   return base + ((ks * E + e) * Mp + n) * (IRL + 1) + irl;
 }
 
-// After every CTA of the cluster pushed its partials: the cluster barrier, then the sums and
-// the epilogue of this CTA's item rows.
+// Receive-buffer slot of tile row `rl` for activation row n when one CTA holds the whole
+// sum of the tile (KS = 1; same layout as epi_dest).
+template <int EPI, int ROWS>
+__device__ __forceinline__ float* epi_dest_local(float* recv, int Mp, int rl, int n) {
+  constexpr int IR = ROWS / epi_elems<EPI>();
+  int e;
+  const int irow = epi_item_row<EPI>(rl, e);
+  return recv + (e * Mp + n) * (IR + 1) + irow;
+}
+
+// The sums of this CTA's item rows over the KS partials in `recv` and the fused epilogue,
+// by threads t0, t0 + nt, ... of the CTA.
 template <int WF, int EPI, int ROWS>
-__device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, int KS, int ks, int R0) {
+__device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv, int KS, int ks, int R0, int t0,
+                                               int nt) {
   auto lora_delta = [](const QArgs& aa, int n, int reg, int col, int width) {
     constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
     return lora_delta_r<R>(aa, n, reg, col, width);
   };
   constexpr int E = epi_elems<EPI>();
   constexpr int IR = ROWS / E;
-  cg::this_cluster().sync();
   const int IRL = IR / KS;
   const int IRL_LOG = __ffs(IRL) - 1;
   const int Mp = epi_mp(a.M);
@@ -156,7 +172,7 @@ __device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, 
     return v;
   };
   if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    for (int i = t0; i < items; i += nt) {
       const int irl = i & (IRL - 1), n = i >> IRL_LOG;
       const int row = R0 + ks * IRL + irl;
       if (row >= a.N) continue;
@@ -175,7 +191,7 @@ __device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, 
     }
   } else if (EPI == EPI_SWIGLU) {
     const int F = a.N >> 1;
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    for (int i = t0; i < items; i += nt) {
       const int irl = i & (IRL - 1), n = i >> IRL_LOG;
       const int j = (R0 >> 1) + ks * IRL + irl;
       if (j >= F) continue;
@@ -190,7 +206,7 @@ __device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, 
     }
   } else {  // EPI_QKV
     const int half_hd = a.hd >> 1;
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    for (int i = t0; i < items; i += nt) {
       const int irl = i & (IRL - 1), n = i >> IRL_LOG;
       const int row = R0 + 2 * (ks * IRL + irl);
       if (row >= a.N) continue;
@@ -226,6 +242,14 @@ __device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, 
       }
     }
   }
+}
+
+// After every CTA of the cluster pushed its partials: the cluster barrier, then the sums and
+// the epilogue of this CTA's item rows.
+template <int WF, int EPI, int ROWS>
+__device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, int KS, int ks, int R0) {
+  cg::this_cluster().sync();
+  qgemm_epilogue<WF, EPI, ROWS>(a, recv, KS, ks, R0, threadIdx.x, blockDim.x);
 }
 
 }  // namespace orch

@@ -25,131 +25,14 @@
 //
 // Every mbarrier wait is bounded (~2 s of globaltimer); on expiry the CTA records
 // ORCH device check bit 8, stops issuing, drains what it issued and frees its TMEM.
-#include <cuda.h>
-
 #include <algorithm>
 #include <cstdlib>
 
-#include "async_copy.cuh"
-#include "qgemm.cuh"
+#include "tcgen05.cuh"
 
 namespace orch {
 
-constexpr int kTcRows = 128;
-constexpr int kTcBK = 128;  // k per stage: two 128-byte swizzle atoms of fp16
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D (TMEM) += A (TMEM, K-major: row i in lane i, two fp16 of consecutive k per column) . B (smem)
-__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Thirty-two consecutive 32-bit columns of this thread's TMEM lane; waits for completion.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
-      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
-      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-// Sixteen consecutive 32-bit columns of this thread's TMEM lane; waits for completion.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);  // start address
-  d |= (uint64_t)1 << 16;                    // leading byte offset (unused: swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset
-  d |= (uint64_t)1 << 46;                    // descriptor version
-  d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
-  return d;
-}
-
-// Eight packed nibbles (k .. k+7) -> eight fp16 (q - 8) * scale in natural k order.
-__device__ __forceinline__ uint4 dq8_natural(uint32_t w, uint32_t sc) {
-  const __half2 s2 = bits_h2(sc);
-  const __half2 magic_sub = bits_h2(0x64086408u);
-  const __half2 p04 = __hmul2(__hsub2(bits_h2(lop3_and_or(w, 0x000F000Fu, 0x64006400u)), magic_sub), s2);
-  const __half2 p15 = __hmul2(
-      __hfma2(bits_h2(lop3_and_or(w, 0x00F000F0u, 0x64006400u)), bits_h2(0x2C002C00u), bits_h2(0xD480D480u)), s2);
-  const uint32_t v = w >> 8;
-  const __half2 p26 = __hmul2(__hsub2(bits_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u)), magic_sub), s2);
-  const __half2 p37 = __hmul2(
-      __hfma2(bits_h2(lop3_and_or(v, 0x00F000F0u, 0x64006400u)), bits_h2(0x2C002C00u), bits_h2(0xD480D480u)), s2);
-  uint4 o;
-  o.x = prmt(h2_bits(p04), h2_bits(p15), 0x5410);  // k0 k1
-  o.y = prmt(h2_bits(p26), h2_bits(p37), 0x5410);  // k2 k3
-  o.z = prmt(h2_bits(p04), h2_bits(p15), 0x7632);  // k4 k5
-  o.w = prmt(h2_bits(p26), h2_bits(p37), 0x7632);  // k6 k7
-  return o;
-}
-
-// Eight nibbles of the tiled layout (stored k0 k2 k4 k6 k1 k3 k5 k7) -> eight fp16
-// (q - 8) * scale in natural k order, with no byte permutes.
-__device__ __forceinline__ uint4 dq8_tiled(uint32_t w, uint32_t sc) {
-  const __half2 s2 = bits_h2(sc);
-  const __half2 magic_sub = bits_h2(0x64086408u);
-  const __half2 hi_mul = bits_h2(0x2C002C00u), hi_add = bits_h2(0xD480D480u);
-  const uint32_t v = w >> 8;
-  uint4 o;
-  o.x = h2_bits(__hmul2(__hsub2(bits_h2(lop3_and_or(w, 0x000F000Fu, 0x64006400u)), magic_sub), s2));
-  o.y = h2_bits(__hmul2(__hfma2(bits_h2(lop3_and_or(w, 0x00F000F0u, 0x64006400u)), hi_mul, hi_add), s2));
-  o.z = h2_bits(__hmul2(__hsub2(bits_h2(lop3_and_or(v, 0x000F000Fu, 0x64006400u)), magic_sub), s2));
-  o.w = h2_bits(__hmul2(__hfma2(bits_h2(lop3_and_or(v, 0x00F000F0u, 0x64006400u)), hi_mul, hi_add), s2));
-  return o;
-}
-
-constexpr int kSub = 64;                           // k per swizzle atom / tiled stage
-constexpr int kWBytes = kTcRows * (kTcBK / 2);     // packed INT4 tile: 128 rows x 64 bytes
-constexpr int kSBytes = kTcRows * 16;              // scales of a 256-k block: 128 rows x 8 fp16
 constexpr int kSRing = 4;
-constexpr int kWarpsDq = 8;                       // dequantisation warps (0-3 also run the epilogue)
 constexpr int kWarpProdW = kWarpsDq;              // TMA producer of weights and scales
 constexpr int kWarpProdX = kWarpsDq + 1;          // TMA producer of activations
 constexpr int kWarpMma = kWarpsDq + 2;            // MMA issuer
@@ -198,7 +81,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
                     const __grid_constant__ CUtensorMap tms, const QArgs a0) {
   using C = TcCfg<NTILE>;
   extern __shared__ __align__(1024) uint8_t smraw[];
-  constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NTILE >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+  constexpr uint32_t kIdesc = umma_idesc_f16<NTILE>();
 
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~(uintptr_t)1023);
   uint8_t* sX = sm + C::OffX;
@@ -429,32 +312,6 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
 // ------------------------------------------------------------------------------------------
 namespace {
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return (EncodeTiledFn) nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-bool encode2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
-  const cuuint64_t gdim[2] = {inner, outer};
-  const cuuint64_t gstride[1] = {row_bytes};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  return encode_fn()(map, dt, 2, const_cast<void*>(base), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <int EPI, int NTILE, int LAY>
 int tc_launch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& ms, const QArgs& a, int KS,
               cudaStream_t st) {
@@ -495,6 +352,10 @@ int tc_dispatch(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap&
 
 template <int EPI>
 int tc_qgemm_run(QArgs a, cudaStream_t st) {
+  if (a.tiled && a.M <= 64) {  // batched decode: persistent stream-K kernel
+    const int rc = tc_sk_run<EPI>(a, st);
+    if (rc != ORCH_ERR_UNSUPPORTED) return rc;
+  }
   // Reference layout: tensor maps need 16-byte row strides, so K % 256 == 0 for the scale
   // rows. Tiled layout: any K % 32 == 0 (the layout is padded to 256).
   const bool tiled = a.tiled != 0;

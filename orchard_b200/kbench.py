@@ -25,13 +25,25 @@ DECODE_SHAPES = [("qkv", 4096, 12288), ("o", 4096, 4096), ("gate_up", 4096, 2201
 L2_BYTES = 126 * 1024 * 1024
 
 
+_SIDE = {}
+
+
+def _capture_stream() -> torch.cuda.Stream:
+    """One capture stream per device for every timed graph (the library keeps per-stream
+    workspaces, so a fresh stream per case would allocate a new one each time)."""
+    d = torch.cuda.current_device()
+    if d not in _SIDE:
+        _SIDE[d] = torch.cuda.Stream()
+    return _SIDE[d]
+
+
 def _graph_time(run, n: int, reps: int) -> float:
     """Microseconds per launch: `reps` launches (rotating over `n` inputs) captured in one
     CUDA graph and replayed, so host launch overhead is not measured."""
     for i in range(2 * n):
         run(i)
     torch.cuda.synchronize()
-    side = torch.cuda.Stream()
+    side = _capture_stream()
     side.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=side):
