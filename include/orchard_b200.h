@@ -202,10 +202,10 @@ int orch_attention_decode(const void* q, const void* k_cache, const void* v_cach
  * kernel. 0 disables the tensor-core kernel. Default 17 (ORCHARD_TC_MIN_M overrides). */
 int orch_set_tc_min_m(uint32_t m);
 /* Batched-decode INT4 GEMMs on tiled weights (orch_q4t_*, 9..64 activation rows): mode 0
- * always uses the per-tile tensor-core kernel, 1 the persistent stream-K kernel (work split
- * evenly over two CTAs per SM, split tiles summed by a fix-up pass), 2 (default) picks
+ * (default) always uses the per-tile tensor-core kernel, 1 the persistent stream-K kernel
+ * (work split evenly over two CTAs per SM, split tiles summed by a fix-up pass), 2 picks
  * stream-K for shapes whose tile count lands between one and one and a half waves of SMs.
- * ORCHARD_TC_SK=0/1 in the environment sets the initial mode. */
+ * ORCHARD_TC_SK=0/1/2 in the environment sets the initial mode. */
 int orch_set_stream_k(int mode);
 /* Vocabulary-split greedy sampling (no reference counterpart: the reference samples on the
  * host, orchard/model.py:244-252). orch_argmax_pairs writes, per row of a logits slice
