@@ -19,9 +19,11 @@
 //    B (activations) from shared memory; tcgen05.commit releases the activation and A
 //    slots. Each handshake is one elected arrival per warp.
 // Decode tiles (NTILE <= 64) use half the tensor memory and ~105 KB of shared memory, so
-// two CTAs share an SM. After the K loop the accumulator is read with tcgen05.ld and handed
-// to the same split-K (cluster / distributed shared memory) reduction and fused epilogues as
-// the mma.sync kernel (qgemm.cuh). TMA loads never use multicast.
+// two CTAs share an SM. After the K loop the accumulator is read with tcgen05.ld: a CTA that
+// holds the whole K range runs the fused epilogue straight from registers (tc_epilogue16);
+// with K split over a cluster the partials go through the same distributed-shared-memory
+// reduction and fused epilogues as the mma.sync kernel (qgemm.cuh). TMA loads never use
+// multicast.
 //
 // Every mbarrier wait is bounded (~2 s of globaltimer); on expiry the CTA records
 // ORCH device check bit 8, stops issuing, drains what it issued and frees its TMEM.
@@ -266,13 +268,49 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   done_ok = mbar_wait(done, 0);
   tc_fence_after();
 
+  const int mcount = min(NTILE, a0.M - tok0);
+  const bool bad = *failed || !done_ok;
+  const int Mp = epi_mp(mcount);
+  QArgs a = a0;
+  a.M = mcount;
+  constexpr int LR = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
+  if (a.lora_t) a.lora_t = a0.lora_t + (size_t)tok0 * LR * a0.lora_r;
+  if (EPI == EPI_STORE || EPI == EPI_RESID) {
+    const size_t os = (EPI == EPI_RESID || a0.out_f32) ? 4 : 2;
+    a.out = static_cast<char*>(a0.out) + (size_t)tok0 * a0.ldo * os;
+  } else if (EPI == EPI_SWIGLU) {
+    a.out = static_cast<__half*>(a0.out) + (size_t)tok0 * (a0.N >> 1);
+  } else {
+    a.out = static_cast<__half*>(a0.out) + (size_t)tok0 * a0.H;
+    a.pos = a0.pos + tok0;
+    if (a0.slots) a.slots = a0.slots + tok0;
+  }
+
+  if (KS == 1) {
+    // The CTA holds the whole sum: the fused epilogue straight from tensor memory, 16
+    // activation rows at a time (warp w owns TMEM lanes / weight rows 32w .. + 31).
+    if (warp < 4 && !bad) {
+#pragma unroll 1
+      for (int cc = 0; cc < Mp; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem_d + ((uint32_t)(32 * warp) << 16) + (uint32_t)cc, r);
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+        tc_epilogue16<EPI>(a, R0, warp, lane, v, cc);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem_d, C::kTmemCols);
+    if (tid == 0 && bad) atomicOr(a0.check, 256u);
+    return;
+  }
+
   // accumulator rows -> owners' receive buffers (they alias the rings: wait for the cluster)
   cg::cluster_group cl = cg::this_cluster();
   cl.sync();
   float* recv = reinterpret_cast<float*>(sm);
-  const int mcount = min(NTILE, a0.M - tok0);
-  const bool bad = *failed || !done_ok;
-  const int Mp = epi_mp(mcount);
   if (warp < 4) {  // TMEM lanes 32w..32w+31 belong to warp w (w = 0..3)
 #pragma unroll 1
     for (int cc = 0; cc < Mp; cc += 16) {
@@ -289,21 +327,6 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, C::kTmemCols);
   if (tid == 0 && bad) atomicOr(a0.check, 256u);
-
-  QArgs a = a0;
-  a.M = mcount;
-  constexpr int LR = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
-  if (a.lora_t) a.lora_t = a0.lora_t + (size_t)tok0 * LR * a0.lora_r;
-  if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    const size_t os = (EPI == EPI_RESID || a0.out_f32) ? 4 : 2;
-    a.out = static_cast<char*>(a0.out) + (size_t)tok0 * a0.ldo * os;
-  } else if (EPI == EPI_SWIGLU) {
-    a.out = static_cast<__half*>(a0.out) + (size_t)tok0 * (a0.N >> 1);
-  } else {
-    a.out = static_cast<__half*>(a0.out) + (size_t)tok0 * a0.H;
-    a.pos = a0.pos + tok0;
-    if (a0.slots) a.slots = a0.slots + tok0;
-  }
   qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0);
 }
 
