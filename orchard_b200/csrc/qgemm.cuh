@@ -151,15 +151,72 @@ __device__ __forceinline__ float* epi_dest_local(float* recv, int Mp, int rl, in
   return recv + (e * Mp + n) * (IR + 1) + irow;
 }
 
+// The fused epilogue of one item for activation row n: idx is the weight row (STORE /
+// RESID), the SwiGLU output column j (v0 = gate, v1 = up), or the even row of a RoPE pair
+// (QKV: v0, v1 = rows idx, idx + 1). The caller checks idx against the output's extent.
+// Every GEMM path ends here, so the epilogue arithmetic has one statement.
+template <int WF, int EPI>
+__device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float v0, float v1) {
+  constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
+  if (EPI == EPI_STORE || EPI == EPI_RESID) {
+    if (WF == W_Q8PC) v0 *= __half2float(a.s[idx]);
+    if (a.lora_t != nullptr) v0 += lora_delta_r<R>(a, n, 0, idx, a.N);
+    const size_t o = (size_t)n * a.ldo + idx;
+    if (EPI == EPI_RESID) {
+      float* y = static_cast<float*>(a.out);
+      y[o] = y[o] + v0;
+    } else if (a.out_f32) {
+      static_cast<float*>(a.out)[o] = v0;
+    } else {
+      static_cast<__half*>(a.out)[o] = __float2half_rn(v0);
+    }
+  } else if (EPI == EPI_SWIGLU) {
+    const int F = a.N >> 1;
+    if (a.lora_t != nullptr) {
+      v0 += lora_delta_r<R>(a, n, 0, idx, F);
+      v1 += lora_delta_r<R>(a, n, 1, idx, F);
+    }
+    const float si = v0 / (1.0f + expf(-v0));
+    static_cast<__half*>(a.out)[(size_t)n * F + idx] = __float2half_rn(si * v1);
+  } else {  // EPI_QKV
+    const int half_hd = a.hd >> 1;
+    const int region = idx / a.H;
+    const int rr = idx - region * a.H;
+    const int head = rr / a.hd, d = rr - head * a.hd;
+    if (a.lora_t != nullptr) {
+      v0 += lora_delta_r<R>(a, n, region, rr, a.H);
+      v1 += lora_delta_r<R>(a, n, region, rr + 1, a.H);
+    }
+    const int p = a.pos[n];
+    if (p < 0 || p >= a.max_seq || p >= a.max_pos) {
+      atomicOr(a.check, 1u);
+      return;
+    }
+    if (region < 2) {
+      const float cs = a.cos_tab[(size_t)p * half_hd + (d >> 1)];
+      const float sn = a.sin_tab[(size_t)p * half_hd + (d >> 1)];
+      const float r0 = v0 * cs - v1 * sn;
+      const float r1 = v0 * sn + v1 * cs;
+      v0 = r0;
+      v1 = r1;
+    }
+    const __half2 hv = __floats2half2_rn(v0, v1);
+    if (region == 0) {
+      *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
+    } else {
+      const int slot = a.slots ? a.slots[n] : n;
+      __half* cache = region == 1 ? a.kc : a.vc;
+      const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
+      *reinterpret_cast<__half2*>(cache + off) = hv;
+    }
+  }
+}
+
 // The sums of this CTA's item rows over the KS partials in `recv` and the fused epilogue,
 // by threads t0, t0 + nt, ... of the CTA.
 template <int WF, int EPI, int ROWS>
 __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv, int KS, int ks, int R0, int t0,
                                                int nt) {
-  auto lora_delta = [](const QArgs& aa, int n, int reg, int col, int width) {
-    constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
-    return lora_delta_r<R>(aa, n, reg, col, width);
-  };
   constexpr int E = epi_elems<EPI>();
   constexpr int IR = ROWS / E;
   const int IRL = IR / KS;
@@ -171,75 +228,17 @@ __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv
     for (int r = 0; r < KS; ++r) v += recv[((r * E + e) * Mp + n) * (IRL + 1) + irl];
     return v;
   };
-  if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    for (int i = t0; i < items; i += nt) {
-      const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+  for (int i = t0; i < items; i += nt) {
+    const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+    if (EPI == EPI_STORE || EPI == EPI_RESID) {
       const int row = R0 + ks * IRL + irl;
-      if (row >= a.N) continue;
-      float v = total(irl, n, 0);
-      if (WF == W_Q8PC) v *= __half2float(a.s[row]);
-      if (a.lora_t != nullptr) v += lora_delta(a, n, 0, row, a.N);
-      const size_t o = (size_t)n * a.ldo + row;
-      if (EPI == EPI_RESID) {
-        float* y = static_cast<float*>(a.out);
-        y[o] = y[o] + v;
-      } else if (a.out_f32) {
-        static_cast<float*>(a.out)[o] = v;
-      } else {
-        static_cast<__half*>(a.out)[o] = __float2half_rn(v);
-      }
-    }
-  } else if (EPI == EPI_SWIGLU) {
-    const int F = a.N >> 1;
-    for (int i = t0; i < items; i += nt) {
-      const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+      if (row < a.N) epi_apply<WF, EPI>(a, n, row, total(irl, n, 0), 0.f);
+    } else if (EPI == EPI_SWIGLU) {
       const int j = (R0 >> 1) + ks * IRL + irl;
-      if (j >= F) continue;
-      float gt = total(irl, n, 0);
-      float up = total(irl, n, 1);
-      if (a.lora_t != nullptr) {
-        gt += lora_delta(a, n, 0, j, F);
-        up += lora_delta(a, n, 1, j, F);
-      }
-      const float si = gt / (1.0f + expf(-gt));
-      static_cast<__half*>(a.out)[(size_t)n * F + j] = __float2half_rn(si * up);
-    }
-  } else {  // EPI_QKV
-    const int half_hd = a.hd >> 1;
-    for (int i = t0; i < items; i += nt) {
-      const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+      if (j < (a.N >> 1)) epi_apply<WF, EPI>(a, n, j, total(irl, n, 0), total(irl, n, 1));
+    } else {
       const int row = R0 + 2 * (ks * IRL + irl);
-      if (row >= a.N) continue;
-      const int region = row / a.H;
-      const int rr = row - region * a.H;
-      const int head = rr / a.hd, d = rr - head * a.hd;
-      float v0 = total(irl, n, 0), v1 = total(irl, n, 1);
-      if (a.lora_t != nullptr) {
-        v0 += lora_delta(a, n, region, rr, a.H);
-        v1 += lora_delta(a, n, region, rr + 1, a.H);
-      }
-      const int p = a.pos[n];
-      if (p < 0 || p >= a.max_seq || p >= a.max_pos) {
-        atomicOr(a.check, 1u);
-        continue;
-      }
-      if (region < 2) {
-        const float cs = a.cos_tab[(size_t)p * half_hd + (d >> 1)];
-        const float sn = a.sin_tab[(size_t)p * half_hd + (d >> 1)];
-        const float r0 = v0 * cs - v1 * sn;
-        const float r1 = v0 * sn + v1 * cs;
-        v0 = r0;
-        v1 = r1;
-      }
-      const __half2 hv = __floats2half2_rn(v0, v1);
-      if (region == 0) {
-        *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
-      } else {
-        const int slot = a.slots ? a.slots[n] : n;
-        __half* cache = region == 1 ? a.kc : a.vc;
-        const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
-        *reinterpret_cast<__half2*>(cache + off) = hv;
-      }
+      if (row < a.N) epi_apply<WF, EPI>(a, n, row, total(irl, n, 0), total(irl, n, 1));
     }
   }
 }

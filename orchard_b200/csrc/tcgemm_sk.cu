@@ -327,41 +327,53 @@ __global__ void __launch_bounds__(kSkThreads, kSkCtasPerSm)
   if (tid == 0 && (*failed || !done_ok)) atomicOr(a.check, 256u);
 }
 
-// Split tiles: the partial sums of the tile's CTAs added in CTA order (deterministic), then
-// the fused epilogue. One CTA per (tile, 16 activation rows), one thread per weight row; up
-// to four partials' loads in flight per thread. Tiles one CTA summed alone are skipped (the
-// GEMM kernel ran their epilogue).
+// Split tiles: one thread per (activation row n, epilogue item) of a tile; the partials of
+// the tile's CTAs are added in CTA order (deterministic) and the item gets the fused epilogue
+// (epi_apply). Items are weight rows (STORE / RESID), SwiGLU outputs (gate row 32b + i, up
+// row 32b + 16 + i) or RoPE pairs (rows 2p, 2p + 1). blockIdx.x = tile, blockIdx.y = a block
+// of 256 (item, n); up to eight partials' loads are in flight per thread. Tiles one CTA
+// summed alone are skipped (the GEMM kernel ran their epilogue).
 template <int EPI, int NTILE>
-__global__ void __launch_bounds__(kTcRows) sk_fixup_kernel(const QArgs a, const SkWork wk, int G) {
+__global__ void __launch_bounds__(256) sk_fixup_kernel(const QArgs a, const SkWork wk, int G) {
   pdl_wait();  // the GEMM kernel's partials
   pdl_trigger();
-  const int t = blockIdx.x, cc = blockIdx.y * 16;
+  const int t = blockIdx.x;
   const int U = wk.U, nblk = wk.nblk;
   const int ca = sk_cta_of(t * nblk, U, G), cb = sk_cta_of((t + 1) * nblk - 1, U, G);
   if (ca == cb) return;
-  const int rl = threadIdx.x, quarter = rl >> 5, lane = rl & 31;
-  const int Mp = epi_mp(a.M);
-  float sum[16];
+  constexpr int E = epi_elems<EPI>();
+  constexpr int IR = kTcRows / E;
+  const int id = blockIdx.y * 256 + threadIdx.x;  // item + IR n
+  if (id >= IR * a.M) return;
+  const int item = id % IR, n = id / IR;
+  const int r0 = E == 1 ? item : (EPI == EPI_SWIGLU ? (item >> 4) * 32 + (item & 15) : 2 * item);
+  const int r1 = EPI == EPI_SWIGLU ? r0 + 16 : r0 + 1;
+  float v0 = 0.f, v1 = 0.f;
+  for (int c0 = ca; c0 <= cb; c0 += 8) {
+    float p0[8], p1[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) sum[i] = 0.f;
-  for (int c0 = ca; c0 <= cb; c0 += 4) {
-    float v[4][16];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const int c2 = c0 + q;
       const bool live = c2 <= cb;
-      const int slot = 2 * c2 + (live && t == sk_start(c2, U, G) / nblk ? 0 : 1);
-      const float* src = wk.part + ((size_t)(live ? slot : 0) * NTILE + cc) * kTcRows + rl;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[q][i] = live && cc + i < Mp ? __ldcg(src + i * kTcRows) : 0.f;
+      const int slot = live ? 2 * c2 + (t == sk_start(c2, U, G) / nblk ? 0 : 1) : 0;
+      const float* src = wk.part + ((size_t)slot * NTILE + n) * kTcRows;
+      p0[q] = live ? __ldcg(src + r0) : 0.f;
+      p1[q] = live && E == 2 ? __ldcg(src + r1) : 0.f;
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (c0 + q <= cb)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sum[i] += v[q][i];
+    for (int q = 0; q < 8; ++q)
+      if (c0 + q <= cb) {
+        v0 += p0[q];
+        v1 += p1[q];
+      }
   }
-  tc_epilogue16<EPI>(a, t * kTcRows, quarter, lane, sum, cc);
+  const int R0 = t * kTcRows;
+  if (EPI == EPI_SWIGLU) {
+    const int j = (R0 >> 1) + item;
+    if (j < (a.N >> 1)) epi_apply<W_Q4, EPI>(a, n, j, v0, v1);
+  } else if (R0 + r0 < a.N) {
+    epi_apply<W_Q4, EPI>(a, n, R0 + r0, v0, v1);
+  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -462,8 +474,9 @@ int sk_launch(const CUtensorMap& mx, const QArgs& a, const SkWork& wk, int G, cu
   bool split = false;
   for (int c = 0; c < G && !split; ++c) split = (int)(((long long)c * wk.U) / G) % wk.nblk != 0;
   if (split) {
-    const dim3 fgrid((wk.U / wk.nblk), (epi_mp(a.M) + 15) / 16);
-    ORCH_CUDA(launch_k(sk_fixup_kernel<EPI, NTILE>, fgrid, dim3(kTcRows), 0, st, dim3(0, 0, 0), a, wk, G));
+    const int items = (kTcRows / epi_elems<EPI>()) * a.M;
+    const dim3 fgrid(wk.U / wk.nblk, (items + 255) / 256);
+    ORCH_CUDA(launch_k(sk_fixup_kernel<EPI, NTILE>, fgrid, dim3(256), 0, st, dim3(0, 0, 0), a, wk, G));
   }
   return ORCH_OK;
 }

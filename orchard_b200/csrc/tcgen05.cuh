@@ -128,87 +128,26 @@ __device__ __forceinline__ uint4 dq8_tiled(uint32_t w, uint32_t sc) {
 // row rl = 32 quarter + lane of the tile starting at weight row R0, v[i] = sum_k
 // W[R0 + rl][k] x[n0 + i][k]. Pairs of rows meet through shuffles: SwiGLU's gate row 32b + i
 // and up row 32b + 16 + i (lanes i, i + 16 of one warp), a RoPE pair 2p, 2p + 1 (adjacent
-// lanes). Same arithmetic as qgemm_epilogue.
+// lanes); the arithmetic is epi_apply's.
 template <int EPI>
 __device__ __forceinline__ void tc_epilogue16(const QArgs& a, int R0, int quarter, int lane, const float (&v)[16],
                                               int n0) {
   const int rl = quarter * 32 + lane;
   const int M = a.M;
-  if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    const int row = R0 + rl;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int n = n0 + i;
-      if (n < M && row < a.N) {
-        float x = v[i];
-        if (a.lora_t != nullptr) x += lora_delta_r<1>(a, n, 0, row, a.N);
-        const size_t o = (size_t)n * a.ldo + row;
-        if (EPI == EPI_RESID) {
-          float* y = static_cast<float*>(a.out);
-          y[o] = y[o] + x;
-        } else if (a.out_f32) {
-          static_cast<float*>(a.out)[o] = x;
-        } else {
-          static_cast<__half*>(a.out)[o] = __float2half_rn(x);
-        }
-      }
-    }
-  } else if (EPI == EPI_SWIGLU) {
-    const int F = a.N >> 1;
-    const int j = (R0 >> 1) + quarter * 16 + (lane & 15);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int n = n0 + i;
-      const float upv = __shfl_xor_sync(0xffffffffu, v[i], 16);
-      if (n < M && lane < 16 && j < F) {
-        float gt = v[i], up = upv;
-        if (a.lora_t != nullptr) {
-          gt += lora_delta_r<2>(a, n, 0, j, F);
-          up += lora_delta_r<2>(a, n, 1, j, F);
-        }
-        const float si = gt / (1.0f + expf(-gt));
-        static_cast<__half*>(a.out)[(size_t)n * F + j] = __float2half_rn(si * up);
-      }
-    }
-  } else {  // EPI_QKV: even lanes own the rotation pair (row, row + 1)
-    const int row = R0 + rl;
-    const int half_hd = a.hd >> 1;
-    const int region = row / a.H;
-    const int rr = row - region * a.H;
-    const int head = rr / a.hd, d = rr - head * a.hd;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int n = n0 + i;
-      const float v1s = __shfl_xor_sync(0xffffffffu, v[i], 1);
-      if (n < M && (lane & 1) == 0 && row < a.N) {
-        float v0 = v[i], v1 = v1s;
-        if (a.lora_t != nullptr) {
-          v0 += lora_delta_r<3>(a, n, region, rr, a.H);
-          v1 += lora_delta_r<3>(a, n, region, rr + 1, a.H);
-        }
-        const int p = a.pos[n];
-        if (p < 0 || p >= a.max_seq || p >= a.max_pos) {
-          atomicOr(a.check, 1u);
-        } else {
-          if (region < 2) {
-            const float cs = a.cos_tab[(size_t)p * half_hd + (d >> 1)];
-            const float sn = a.sin_tab[(size_t)p * half_hd + (d >> 1)];
-            const float r0 = v0 * cs - v1 * sn;
-            const float r1 = v0 * sn + v1 * cs;
-            v0 = r0;
-            v1 = r1;
-          }
-          const __half2 hv = __floats2half2_rn(v0, v1);
-          if (region == 0) {
-            *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
-          } else {
-            const int slot = a.slots ? a.slots[n] : n;
-            __half* cache = region == 1 ? a.kc : a.vc;
-            const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
-            *reinterpret_cast<__half2*>(cache + off) = hv;
-          }
-        }
-      }
+  for (int i = 0; i < 16; ++i) {
+    const int n = n0 + i;
+    if (EPI == EPI_STORE || EPI == EPI_RESID) {
+      const int row = R0 + rl;
+      if (n < M && row < a.N) epi_apply<W_Q4, EPI>(a, n, row, v[i], 0.f);
+    } else if (EPI == EPI_SWIGLU) {
+      const int j = (R0 >> 1) + quarter * 16 + (lane & 15);
+      const float up = __shfl_xor_sync(0xffffffffu, v[i], 16);
+      if (n < M && lane < 16 && j < (a.N >> 1)) epi_apply<W_Q4, EPI>(a, n, j, v[i], up);
+    } else {
+      const int row = R0 + rl;
+      const float v1 = __shfl_xor_sync(0xffffffffu, v[i], 1);
+      if (n < M && (lane & 1) == 0 && row < a.N) epi_apply<W_Q4, EPI>(a, n, row, v[i], v1);
     }
   }
 }
