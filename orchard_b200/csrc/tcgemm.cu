@@ -19,9 +19,9 @@
 //    B (activations) from shared memory; tcgen05.commit releases the activation and A
 //    slots. Each handshake is one elected arrival per warp.
 // Decode tiles (NTILE <= 64) use half the tensor memory and ~105 KB of shared memory, so
-// two CTAs share an SM. After the K loop the accumulator is read with tcgen05.ld: a CTA that
-// holds the whole K range runs the fused epilogue straight from registers (tc_epilogue16);
-// with K split over a cluster the partials go through the same distributed-shared-memory
+// two CTAs share an SM. After the K loop the accumulator is read with tcgen05.ld: a decode
+// CTA that holds the whole K range runs the fused epilogue straight from registers
+// (tc_epilogue16); otherwise the partials go through the same distributed-shared-memory
 // reduction and fused epilogues as the mma.sync kernel (qgemm.cuh). TMA loads never use
 // multicast.
 //
@@ -286,9 +286,12 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     if (a0.slots) a.slots = a0.slots + tok0;
   }
 
-  if (KS == 1) {
-    // The CTA holds the whole sum: the fused epilogue straight from tensor memory, 16
-    // activation rows at a time (warp w owns TMEM lanes / weight rows 32w .. + 31).
+  if (KS == 1 && C::kDecode) {
+    // The CTA holds the whole sum of a decode tile: the fused epilogue straight from tensor
+    // memory, 16 activation rows at a time (warp w owns TMEM lanes / weight rows 32w .. + 31).
+    // Prefill tiles (128-256 rows) keep the receive-buffer path below, where all eleven warps
+    // share the epilogue (with four warps the LoRA terms of 256 rows took 8x512-token prefill
+    // from 162 to 264 ms).
     if (warp < 4 && !bad) {
 #pragma unroll 1
       for (int cc = 0; cc < Mp; cc += 16) {
