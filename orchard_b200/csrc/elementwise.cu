@@ -394,13 +394,78 @@ __global__ void __launch_bounds__(256) lora_xa_kernel(const __half* x, const flo
     __syncthreads();
   }
 }
+
+// x.A for many rows (prefill): a CTA takes 32 rows and all R <= 64 columns, staging 64-k
+// chunks of x (as fp32) and A in shared memory, so A is read once per 32 rows instead of once
+// per row; the next chunk's loads are in flight (in registers) while the current one is
+// multiplied. Thread (row, column group g) accumulates columns g, g + 8, ..., in fp32 over k
+// in increasing order.
+constexpr int kXaRows = 32, kXaK = 64, kXaCols = 64;
+constexpr int kXaXPer = kXaRows * kXaK / 256, kXaAPer = kXaK * kXaCols / 256;  // loads per thread
+__global__ void __launch_bounds__(256) lora_xa_tiled_kernel(const __half* x, const float* A, float* t, int M, int K,
+                                                           int R) {
+  __shared__ float xs[kXaRows][kXaK + 1];
+  __shared__ float as[kXaK][kXaCols];
+  pdl_trigger();
+  pdl_wait();
+  const int m0 = blockIdx.x * kXaRows;
+  const int tid = threadIdx.x, row = tid >> 3, cgp = tid & 7;
+  float xr[kXaXPer], ar[kXaAPer];
+  auto gload = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < kXaXPer; ++u) {
+      const int i = tid + 256 * u, r = i / kXaK, k = k0 + (i - r * kXaK), m = m0 + r;
+      xr[u] = (m < M && k < K) ? __half2float(x[(size_t)m * K + k]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kXaAPer; ++u) {
+      const int i = tid + 256 * u, kk = i / kXaCols, j = i - kk * kXaCols, k = k0 + kk;
+      ar[u] = (k < K && j < R) ? A[(size_t)k * R + j] : 0.f;
+    }
+  };
+  float acc[kXaCols / 8];
+#pragma unroll
+  for (int i = 0; i < kXaCols / 8; ++i) acc[i] = 0.f;
+  gload(0);
+  for (int k0 = 0; k0 < K; k0 += kXaK) {
+#pragma unroll
+    for (int u = 0; u < kXaXPer; ++u) {
+      const int i = tid + 256 * u, r = i / kXaK;
+      xs[r][i - r * kXaK] = xr[u];
+    }
+#pragma unroll
+    for (int u = 0; u < kXaAPer; ++u) {
+      const int i = tid + 256 * u, kk = i / kXaCols;
+      as[kk][i - kk * kXaCols] = ar[u];
+    }
+    __syncthreads();
+    if (k0 + kXaK < K) gload(k0 + kXaK);
+#pragma unroll 8
+    for (int kk = 0; kk < kXaK; ++kk) {
+      const float xv = xs[row][kk];
+#pragma unroll
+      for (int i = 0; i < kXaCols / 8; ++i) acc[i] = fmaf(xv, as[kk][cgp + 8 * i], acc[i]);
+    }
+    __syncthreads();
+  }
+  const int m = m0 + row;
+#pragma unroll
+  for (int i = 0; i < kXaCols / 8; ++i) {
+    const int j = cgp + 8 * i;
+    if (m < M && j < R) t[(size_t)m * R + j] = acc[i];
+  }
+}
 }  // namespace orch
 
 extern "C" int orch_lora_xa(const void* x, const float* a, float* t, uint32_t M, uint32_t K, uint32_t R,
                             void* stream) {
   if (M == 0 || R == 0) return ORCH_OK;
   ORCH_REQUIRE(x && a && t && K > 0, "lora_xa: bad arguments");
-  ORCH_CUDA(orch::launch_k(orch::lora_xa_kernel, dim3(M), dim3(256), 0, as_stream(stream), dim3(0, 0, 0),
-                           (const __half*)x, a, t, (int)K, (int)R));
+  if (M >= 256 && R <= (uint32_t)orch::kXaCols)  // many rows: A staged once per 32 rows
+    ORCH_CUDA(orch::launch_k(orch::lora_xa_tiled_kernel, dim3((M + orch::kXaRows - 1) / orch::kXaRows), dim3(256), 0,
+                             as_stream(stream), dim3(0, 0, 0), (const __half*)x, a, t, (int)M, (int)K, (int)R));
+  else
+    ORCH_CUDA(orch::launch_k(orch::lora_xa_kernel, dim3(M), dim3(256), 0, as_stream(stream), dim3(0, 0, 0),
+                             (const __half*)x, a, t, (int)K, (int)R));
   return check_launch("lora_xa");
 }

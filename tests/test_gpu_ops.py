@@ -302,3 +302,18 @@ def test_attention_decode(M, L, hd):
         ref = ops.attention_one(q[m].reshape(nh, hd).astype(np.float32), kc[sl, :, :L_m].astype(np.float32),
                                 vc[sl, :, :L_m].astype(np.float32))
         assert rel_err(o[m].reshape(nh, hd), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("M,K,R", [(5, 4096, 48), (300, 4096, 48), (4096, 4096, 48), (1000, 96, 16), (4096, 512, 80)])
+def test_lora_xa(M, K, R):
+    """t = x.A (the first LoRA factor, orchard/model.py:60-76): fp16 x, fp32 A, fp32 t. Small M
+    takes the one-row-per-CTA kernel, M >= 256 with R <= 64 the tiled one; both are fp32 dot
+    products, so max|gpu - ref| / max|ref| <= 1e-5 against fp32 NumPy."""
+    g = np.random.default_rng([31, M, K, R])
+    x = g.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+    a = (g.standard_normal((K, R), dtype=np.float32) * 0.01).astype(np.float32)
+    t = torch.empty((M, R), dtype=torch.float32, device="cuda")
+    call("orch_lora_xa", D(x), D(a), t, M, K, R, S())
+    torch.cuda.synchronize()
+    ref = x.astype(np.float32) @ a
+    assert rel_err(t.cpu().numpy(), ref) <= 1e-5
