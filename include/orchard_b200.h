@@ -201,6 +201,16 @@ int orch_attention_decode(const void* q, const void* k_cache, const void* v_cach
  * kernel (TMEM accumulators, TMA-fed activations); fewer rows use the mma.sync decode
  * kernel. 0 disables the tensor-core kernel. Default 17 (ORCHARD_TC_MIN_M overrides). */
 int orch_set_tc_min_m(uint32_t m);
+/* Causal attention for a prefill chunk (no counterpart in the reference, whose prefill
+ * attention is the per-token host loop of orchard/model.py:112-144). q and out are [M, heads,
+ * 128] fp16, the caches as for orch_attention_decode. `units` (device, 16-byte aligned) lists
+ * num_units records of four int32 (row0, rows, slot, pos0): rows row0 .. row0 + rows - 1
+ * (1..64 of them) belong to cache slot `slot` at positions pos0, pos0 + 1, ..., and their
+ * K/V are already in the cache; each row attends to positions 0..its own. Rows in no unit are
+ * not written. Tensor-core kernel: head_dim 128 only (ORCH_ERR_UNSUPPORTED otherwise). */
+int orch_attention_prefill(const void* q, const void* k_cache, const void* v_cache, const int32_t* units,
+                           uint32_t num_units, void* out, uint32_t M, uint32_t num_heads, uint32_t head_dim,
+                           uint32_t max_seq, void* stream);
 /* Batched-decode INT4 GEMMs on tiled weights (orch_q4t_*, 9..64 activation rows): mode 0
  * (default) always uses the per-tile tensor-core kernel, 1 the persistent stream-K kernel
  * (work split evenly over two CTAs per SM, split tiles summed by a fix-up pass), 2 picks

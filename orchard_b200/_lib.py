@@ -84,6 +84,7 @@ _SIGS = {
     "orch_attention_workspace_bytes": (_sz, [_u32, _u32, _u32, _u32]),
     "orch_attention_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _sz, _vp]),
     "orch_set_tc_min_m": (_i32, [_u32]),
+    "orch_attention_prefill": (_i32, [_vp, _vp, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _u32, _vp]),
     "orch_set_stream_k": (_i32, [_i32]),
     "orch_argmax_pairs": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "orch_argmax_merge": (_i32, [_vp, _u32, _u32, _u32, _u32, _vp, _vp]),

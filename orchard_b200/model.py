@@ -129,6 +129,26 @@ def interleave_gate_up(p1, s1, p3, s3):
     return il(p1, p3).contiguous(), il(s1, s3).contiguous()
 
 
+def prefill_units(positions, slots, max_rows: int = 64) -> np.ndarray:
+    """Work units of orch_attention_prefill for the rows of a prefill chunk: runs of
+    consecutive rows in one cache slot at consecutive positions, cut into pieces of at most
+    `max_rows`; one int32 record (row0, rows, slot, pos0) each."""
+    pos = np.asarray(positions, np.int64)
+    sl = np.asarray(slots, np.int64)
+    n = len(pos)
+    if n == 0:
+        return np.zeros((0, 4), np.int32)
+    brk = np.ones(n, bool)
+    brk[1:] = (sl[1:] != sl[:-1]) | (pos[1:] != pos[:-1] + 1)
+    starts = np.flatnonzero(brk)
+    ends = np.append(starts[1:], n)
+    out = []
+    for a, e in zip(starts.tolist(), ends.tolist()):
+        for r in range(a, e, max_rows):
+            out.append((r, min(max_rows, e - r), sl[r], pos[r]))
+    return np.asarray(out, np.int32).reshape(-1, 4)
+
+
 def tile_q4(w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     """Re-lays a packed INT4 weight (reference layout, on the device) into the tiled layout
     the tensor-core GEMM streams (rows in tiles of 128, k in blocks of 256, each block one
@@ -356,6 +376,9 @@ class DecodeEngine:
         # with the column split one extra slot takes the padding rows of a prefill whose
         # token count is below another rank's (their K/V land there and are never read)
         self.scratch_slot = max_batch if self.split is not None else -1
+        # prefill attention on the tensor-core kernel (head_dim 128); False: the decode kernel
+        # per row (ORCHARD_PREFILL_ATTN=decode)
+        self.prefill_attention = os.environ.get("ORCHARD_PREFILL_ATTN", "tc") != "decode"
         nslots = max_batch + (1 if self.split is not None else 0)
         self.k_cache = torch.zeros((nl, nslots, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
@@ -397,9 +420,11 @@ class DecodeEngine:
         return ptr(bufs.lora_t), ptr(b), self.lora_r
 
     # -- one step ----------------------------------------------------------------------
-    def run_layers(self, M: int, bufs: Optional[RowBuffers] = None):
+    def run_layers(self, M: int, bufs: Optional[RowBuffers] = None, units: Optional[torch.Tensor] = None):
         """All layers for rows [0, M) of `bufs` (default: the decode buffers): token ids in
-        tok_in, positions in pos, cache slots in slots."""
+        tok_in, positions in pos, cache slots in slots. `units` (prefill: a device copy of
+        prefill_units for these rows) routes attention to the tensor-core prefill kernel,
+        which reads each sequence's keys once per 64 rows instead of once per row."""
         b = bufs if bufs is not None else self.dec
         cfg, s = self.cfg, _stream()
         H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
@@ -418,8 +443,12 @@ class DecodeEngine:
                 call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
                      ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
                      self.max_seq, lt, lb, lr, s)
-            call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
-                 ptr(b.attn), M, nh, hd, self.max_seq, ptr(b.attn_ws), b.attn_ws_bytes, s)
+            if units is not None:
+                call("orch_attention_prefill", ptr(b.q), ptr(kc), ptr(vc), ptr(units), units.shape[0],
+                     ptr(b.attn), M, nh, hd, self.max_seq, s)
+            else:
+                call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
+                     ptr(b.attn), M, nh, hd, self.max_seq, ptr(b.attn_ws), b.attn_ws_bytes, s)
             lt, lb, lr = self._lora(L, "o", b.attn, M, s, b)
             if L.tiled:
                 call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
@@ -490,12 +519,16 @@ class DecodeEngine:
         t_d = torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device)
         p_d = torch.as_tensor(np.asarray(positions, np.int32)).to(self.device)
         s_d = torch.as_tensor(np.asarray(slots, np.int32)).to(self.device)
+        pos_h, slots_h = np.asarray(positions, np.int32), np.asarray(slots, np.int32)
         for r0 in range(0, n, rows):
             m = min(rows, n - r0)
             b.tok_in[:m].copy_(t_d[r0:r0 + m])
             b.pos[:m].copy_(p_d[r0:r0 + m])
             b.slots[:m].copy_(s_d[r0:r0 + m])
-            self.run_layers(m, b)
+            units = None
+            if self.prefill_attention and self.cfg.head_dim == 128:
+                units = torch.as_tensor(prefill_units(pos_h[r0:r0 + m], slots_h[r0:r0 + m])).to(self.device)
+            self.run_layers(m, b, units)
 
     def _split_bufs(self, b: RowBuffers) -> _SplitBuffers:
         if self.spre is None or self.spre.x is not b.x:
