@@ -374,6 +374,7 @@ int qgemm_run(QArgs a, cudaStream_t st) {
       b.out = static_cast<__half*>(a.out) + (size_t)m0 * a.H;
       b.pos = a.pos + m0;
       if (a.slots) b.slots = a.slots + m0;
+      else b.slot0 = a.slot0 + m0;
     }
     const int rc = dispatch_nt<WF, EPI>(b, KS, smem, st);
     if (rc != ORCH_OK) return rc;

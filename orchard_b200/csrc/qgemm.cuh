@@ -43,7 +43,8 @@ struct QArgs {
   // QKV + RoPE + KV append
   int H, nh, hd, max_seq, max_pos;
   const int* pos;
-  const int* slots;
+  const int* slots;   // cache slot of each row; null: row index (slot0 + local row)
+  int slot0;          // with null slots, the first row's index (row blocks advance it)
   const float* cos_tab;
   const float* sin_tab;
   __half* kc;
@@ -155,12 +156,27 @@ __device__ __forceinline__ float* epi_dest_local(float* recv, int Mp, int rl, in
 // RESID), the SwiGLU output column j (v0 = gate, v1 = up), or the even row of a RoPE pair
 // (QKV: v0, v1 = rows idx, idx + 1). The caller checks idx against the output's extent.
 // Every GEMM path ends here, so the epilogue arithmetic has one statement.
-template <int WF, int EPI>
-__device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float v0, float v1) {
-  constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
+template <int EPI>
+struct LoraGlobal {  // the LoRA term from the operands in global memory
+  const QArgs& a;
+  __device__ __forceinline__ float operator()(int n, int reg, int col, int width) const {
+    constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
+    return lora_delta_r<R>(a, n, reg, col, width);
+  }
+};
+
+// STORE / RESID: the value of output (n, row idx) before it is stored or added.
+template <int WF, typename LoraF>
+__device__ __forceinline__ float epi_value(const QArgs& a, int n, int idx, float v0, const LoraF& lora) {
+  if (WF == W_Q8PC) v0 *= __half2float(a.s[idx]);
+  if (a.lora_t != nullptr) v0 += lora(n, 0, idx, a.N);
+  return v0;
+}
+
+template <int WF, int EPI, typename LoraF>
+__device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float v0, float v1, const LoraF& lora) {
   if (EPI == EPI_STORE || EPI == EPI_RESID) {
-    if (WF == W_Q8PC) v0 *= __half2float(a.s[idx]);
-    if (a.lora_t != nullptr) v0 += lora_delta_r<R>(a, n, 0, idx, a.N);
+    v0 = epi_value<WF>(a, n, idx, v0, lora);
     const size_t o = (size_t)n * a.ldo + idx;
     if (EPI == EPI_RESID) {
       float* y = static_cast<float*>(a.out);
@@ -173,8 +189,8 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
   } else if (EPI == EPI_SWIGLU) {
     const int F = a.N >> 1;
     if (a.lora_t != nullptr) {
-      v0 += lora_delta_r<R>(a, n, 0, idx, F);
-      v1 += lora_delta_r<R>(a, n, 1, idx, F);
+      v0 += lora(n, 0, idx, F);
+      v1 += lora(n, 1, idx, F);
     }
     const float si = v0 / (1.0f + expf(-v0));
     static_cast<__half*>(a.out)[(size_t)n * F + idx] = __float2half_rn(si * v1);
@@ -184,8 +200,8 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
     const int rr = idx - region * a.H;
     const int head = rr / a.hd, d = rr - head * a.hd;
     if (a.lora_t != nullptr) {
-      v0 += lora_delta_r<R>(a, n, region, rr, a.H);
-      v1 += lora_delta_r<R>(a, n, region, rr + 1, a.H);
+      v0 += lora(n, region, rr, a.H);
+      v1 += lora(n, region, rr + 1, a.H);
     }
     const int p = a.pos[n];
     if (p < 0 || p >= a.max_seq || p >= a.max_pos) {
@@ -204,7 +220,7 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
     if (region == 0) {
       *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
     } else {
-      const int slot = a.slots ? a.slots[n] : n;
+      const int slot = a.slots ? a.slots[n] : a.slot0 + n;
       __half* cache = region == 1 ? a.kc : a.vc;
       const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
       *reinterpret_cast<__half2*>(cache + off) = hv;
@@ -212,11 +228,16 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
   }
 }
 
+template <int WF, int EPI>
+__device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float v0, float v1) {
+  epi_apply<WF, EPI>(a, n, idx, v0, v1, LoraGlobal<EPI>{a});
+}
+
 // The sums of this CTA's item rows over the KS partials in `recv` and the fused epilogue,
-// by threads t0, t0 + nt, ... of the CTA.
-template <int WF, int EPI, int ROWS>
+// by threads t0, t0 + nt, ... of the CTA (LoRA terms from `lora`).
+template <int WF, int EPI, int ROWS, typename LoraF>
 __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv, int KS, int ks, int R0, int t0,
-                                               int nt) {
+                                               int nt, const LoraF& lora) {
   constexpr int E = epi_elems<EPI>();
   constexpr int IR = ROWS / E;
   const int IRL = IR / KS;
@@ -228,19 +249,50 @@ __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv
     for (int r = 0; r < KS; ++r) v += recv[((r * E + e) * Mp + n) * (IRL + 1) + irl];
     return v;
   };
+  if (EPI == EPI_RESID) {
+    // residual read-modify-writes eight at a time: their loads are issued together instead of
+    // one dependent round trip per output (the compiler cannot tell the stores from the loads)
+    float* y = static_cast<float*>(a.out);
+    for (int i0 = t0; i0 < items; i0 += 8 * nt) {
+      float v[8], yv[8];
+      size_t o[8];
+      bool live[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * nt;
+        const int irl = i & (IRL - 1), n = i >> IRL_LOG;
+        const int row = R0 + ks * IRL + irl;
+        live[u] = i < items && row < a.N;
+        o[u] = live[u] ? (size_t)n * a.ldo + row : 0;
+        v[u] = live[u] ? epi_value<WF>(a, n, row, total(irl, n, 0), lora) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) yv[u] = live[u] ? y[o[u]] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (live[u]) y[o[u]] = yv[u] + v[u];
+    }
+    return;
+  }
   for (int i = t0; i < items; i += nt) {
     const int irl = i & (IRL - 1), n = i >> IRL_LOG;
     if (EPI == EPI_STORE || EPI == EPI_RESID) {
       const int row = R0 + ks * IRL + irl;
-      if (row < a.N) epi_apply<WF, EPI>(a, n, row, total(irl, n, 0), 0.f);
+      if (row < a.N) epi_apply<WF, EPI>(a, n, row, total(irl, n, 0), 0.f, lora);
     } else if (EPI == EPI_SWIGLU) {
       const int j = (R0 >> 1) + ks * IRL + irl;
-      if (j < (a.N >> 1)) epi_apply<WF, EPI>(a, n, j, total(irl, n, 0), total(irl, n, 1));
+      if (j < (a.N >> 1)) epi_apply<WF, EPI>(a, n, j, total(irl, n, 0), total(irl, n, 1), lora);
     } else {
       const int row = R0 + 2 * (ks * IRL + irl);
-      if (row < a.N) epi_apply<WF, EPI>(a, n, row, total(irl, n, 0), total(irl, n, 1));
+      if (row < a.N) epi_apply<WF, EPI>(a, n, row, total(irl, n, 0), total(irl, n, 1), lora);
     }
   }
+}
+
+template <int WF, int EPI, int ROWS>
+__device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv, int KS, int ks, int R0, int t0,
+                                               int nt) {
+  qgemm_epilogue<WF, EPI, ROWS>(a, recv, KS, ks, R0, t0, nt, LoraGlobal<EPI>{a});
 }
 
 // After every CTA of the cluster pushed its partials: the cluster barrier, then the sums and
@@ -249,6 +301,12 @@ template <int WF, int EPI, int ROWS>
 __device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, int KS, int ks, int R0) {
   cg::this_cluster().sync();
   qgemm_epilogue<WF, EPI, ROWS>(a, recv, KS, ks, R0, threadIdx.x, blockDim.x);
+}
+template <int WF, int EPI, int ROWS, typename LoraF>
+__device__ __forceinline__ void qgemm_finish(const QArgs& a, const float* recv, int KS, int ks, int R0,
+                                             const LoraF& lora) {
+  cg::this_cluster().sync();
+  qgemm_epilogue<WF, EPI, ROWS>(a, recv, KS, ks, R0, threadIdx.x, blockDim.x, lora);
 }
 
 }  // namespace orch

@@ -75,6 +75,22 @@ struct TcCfg {
   static_assert(XSub % 1024 == 0, "swizzle atoms are 1024-byte aligned");
 };
 
+// LoRA terms of one prefill tile from shared memory: the tile's slice of t (the regions it
+// touches, all its activation rows) and of B (those regions, its columns), staged once after
+// the K loop instead of 2r global loads per output. Same FMA order as lora_delta_r.
+struct LoraSmem {
+  const float* ts;  // [region][Mp][r]
+  const float* bs;  // [region][r][cw]
+  int reg0, c0, cw, r, Mp;
+  __device__ __forceinline__ float operator()(int n, int reg, int col, int width) const {
+    const float* t = ts + ((size_t)(reg - reg0) * Mp + n) * r;
+    const float* b = bs + (size_t)(reg - reg0) * r * cw + (col - c0);
+    float v = 0.f;
+    for (int q = 0; q < r; ++q) v = fmaf(t[q], b[q * cw], v);
+    return v;
+  }
+};
+
 // LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 64 bytes.
 // LAY 1: weights in the tiled layout (qgemm.cuh), read by contiguous 8 KB bulk copies.
 template <int EPI, int NTILE, int LAY>
@@ -284,6 +300,7 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     a.out = static_cast<__half*>(a0.out) + (size_t)tok0 * a0.H;
     a.pos = a0.pos + tok0;
     if (a0.slots) a.slots = a0.slots + tok0;
+    else a.slot0 = a0.slot0 + tok0;
   }
 
   if (KS == 1 && C::kDecode) {
@@ -330,6 +347,33 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, C::kTmemCols);
   if (tid == 0 && bad) atomicOr(a0.check, 256u);
+  if (!C::kDecode && a.lora_t != nullptr) {
+    // prefill tiles: stage the LoRA operands of this tile beyond the receive buffer
+    constexpr int RR = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
+    const int reg0 = EPI == EPI_QKV ? R0 / a.H : 0;
+    const int nreg = EPI == EPI_SWIGLU ? 2 : 1;
+    const int c0 = EPI == EPI_QKV ? R0 - reg0 * a.H : (EPI == EPI_SWIGLU ? R0 >> 1 : R0);
+    const int cw = EPI == EPI_SWIGLU ? kTcRows / 2 : kTcRows;
+    const int width = EPI == EPI_QKV ? a.H : (EPI == EPI_SWIGLU ? a.N >> 1 : a.N);
+    const int r = a.lora_r;
+    const int recv_floats = epi_recv_floats<kTcRows>(mcount);
+    const size_t need = (size_t)nreg * r * (Mp + cw) * sizeof(float);
+    if ((EPI != EPI_QKV || c0 + kTcRows <= a.H) && (size_t)recv_floats * 4 + need <= (size_t)C::OffBar) {
+      float* ts = recv + recv_floats;
+      float* bs = ts + (size_t)nreg * Mp * r;
+      for (int i = tid; i < nreg * Mp * r; i += kTcThreads2) {
+        const int g = i / (Mp * r), rem = i - g * Mp * r, n = rem / r, q = rem - n * r;
+        ts[i] = n < mcount ? a.lora_t[((size_t)n * RR + reg0 + g) * r + q] : 0.f;
+      }
+      for (int i = tid; i < nreg * r * cw; i += kTcThreads2) {
+        const int g = i / (r * cw), rem = i - g * r * cw, q = rem / cw, col = c0 + (rem - q * cw);
+        bs[i] = col < width ? a.lora_b[((size_t)(reg0 + g) * r + q) * width + col] : 0.f;
+      }
+      // qgemm_finish's cluster barrier orders these stores before the epilogue reads them
+      qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0, LoraSmem{ts, bs, reg0, c0, cw, r, Mp});
+      return;
+    }
+  }
   qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0);
 }
 

@@ -101,3 +101,48 @@ def test_tc_fused_epilogues_match_mma_path(M):
         outs.append([t.float().cpu().numpy() for t in (q, kc, vc, h, r)])
     for a, b in zip(*outs):
         assert rel_err(a, b) <= 5e-3
+
+
+def test_tc_fused_epilogues_with_lora_prefill_rows():
+    """Prefill-sized batch (a full 256-row tile and a partial one) with rank-16 LoRA terms on
+    the three fused entry points: the tensor-core kernel (LoRA operands staged in shared
+    memory after the K loop) against the mma.sync kernel (LoRA operands read from global
+    memory); same kernel-to-kernel tolerance as above."""
+    M, H, F, nh, hd, max_seq, r = 300, 4096, 11008, 32, 128, 512, 16
+    g = np.random.default_rng([10, M])
+    pq, sq, _ = weights(3 * H, H)
+    p13, s13, _ = weights(2 * F, H)
+    p2, s2, _ = weights(H, F)
+    x = g.standard_normal((M, H), dtype=np.float32).astype(np.float16)
+    h_in = g.standard_normal((M, F), dtype=np.float32).astype(np.float16)
+    pos = torch.tensor(np.arange(M) % max_seq, dtype=torch.int32, device="cuda")
+    c, sn = ops.precompute_freqs_cis(hd, 2048)
+    cd, sd = torch.from_numpy(c).cuda(), torch.from_numpy(sn).cuda()
+
+    def lora(regions, width):
+        t = torch.from_numpy(g.standard_normal((M, regions, r), dtype=np.float32) * 0.1).cuda()
+        b = torch.from_numpy(g.standard_normal((regions, r, width), dtype=np.float32) * 0.1).cuda()
+        return t, b
+
+    lt3, lb3 = lora(3, H)
+    lt2, lb2 = lora(2, F)
+    lt1, lb1 = lora(1, H)
+    outs = []
+    for tc in (1, 0):
+        call("orch_set_tc_min_m", tc)
+        q = torch.zeros((M, H), dtype=torch.float16, device="cuda")
+        kc = torch.zeros((M, nh, max_seq, hd), dtype=torch.float16, device="cuda")
+        vc = torch.zeros_like(kc)
+        call("orch_q4_qkv_rope", torch.from_numpy(pq).cuda(), torch.from_numpy(sq).cuda(), torch.from_numpy(x).cuda(),
+             M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, lt3, lb3, r, S())
+        h = torch.zeros((M, F), dtype=torch.float16, device="cuda")
+        call("orch_q4_linear_swiglu", torch.from_numpy(p13).cuda(), torch.from_numpy(s13).cuda(),
+             torch.from_numpy(x).cuda(), h, M, H, F, lt2, lb2, r, S())
+        res = torch.ones((M, H), dtype=torch.float32, device="cuda")
+        call("orch_q4_linear_resid", torch.from_numpy(p2).cuda(), torch.from_numpy(s2).cuda(),
+             torch.from_numpy(h_in).cuda(), res, M, F, H, lt1, lb1, r, S())
+        torch.cuda.synchronize()
+        outs.append([t.float().cpu().numpy() for t in (q, kc, vc, h, res)])
+    call("orch_set_tc_min_m", 17)
+    for a, b in zip(*outs):
+        assert rel_err(a, b) <= 5e-3
