@@ -249,9 +249,10 @@ __device__ __forceinline__ void qgemm_epilogue(const QArgs& a, const float* recv
     for (int r = 0; r < KS; ++r) v += recv[((r * E + e) * Mp + n) * (IRL + 1) + irl];
     return v;
   };
-  if (EPI == EPI_RESID) {
-    // residual read-modify-writes eight at a time: their loads are issued together instead of
-    // one dependent round trip per output (the compiler cannot tell the stores from the loads)
+  if (EPI == EPI_RESID && items >= 8 * nt) {
+    // prefill-sized tiles: residual read-modify-writes eight at a time, their loads issued
+    // together instead of one dependent round trip per output (the compiler cannot tell the
+    // stores from the loads); with a few items per thread (decode) the plain loop is faster
     float* y = static_cast<float*>(a.out);
     for (int i0 = t0; i0 < items; i0 += 8 * nt) {
       float v[8], yv[8];
