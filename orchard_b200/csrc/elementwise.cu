@@ -395,65 +395,141 @@ __global__ void __launch_bounds__(256) lora_xa_kernel(const __half* x, const flo
   }
 }
 
-// x.A for many rows (prefill): a CTA takes 32 rows and all R <= 64 columns, staging 64-k
-// chunks of x (as fp32) and A in shared memory, so A is read once per 32 rows instead of once
-// per row; the next chunk's loads are in flight (in registers) while the current one is
-// multiplied. Thread (row, column group g) accumulates columns g, g + 8, ..., in fp32 over k
-// in increasing order.
-constexpr int kXaRows = 32, kXaK = 64, kXaCols = 64;
-constexpr int kXaXPer = kXaRows * kXaK / 256, kXaAPer = kXaK * kXaCols / 256;  // loads per thread
-__global__ void __launch_bounds__(256) lora_xa_tiled_kernel(const __half* x, const float* A, float* t, int M, int K,
-                                                           int R) {
-  __shared__ float xs[kXaRows][kXaK + 1];
-  __shared__ float as[kXaK][kXaCols];
+// x.A for many rows (prefill) on the tensor cores: mma.sync m16n8k8 with TF32 operands.
+// x is fp16, exact in TF32; A (fp32) is split into two TF32 terms, big = round(A) and
+// small = round(A - big), so x.A = x.big + x.small keeps ~22 bits of A with fp32's exponent
+// range. The tensor core adds its products into the accumulator with less care than an fp32
+// add (K = 4096 in one accumulator drifted 2e-5 of max|t|), so every 16 k start a fresh
+// accumulator that is added into the running fp32 sums with a plain (round-to-nearest) add.
+// A CTA takes 32 rows and NC >= R columns; its 8 warps are 2 row groups of 16 x 4 quarters
+// of each 64-k chunk, the quarters summed in a fixed order at the end. x and A chunks stream
+// through a 6-stage cp.async ring (5 chunks in flight while one is multiplied).
+constexpr int kXaRows = 32, kXaK = 64, kXaStages = 6, kXaThreads = 256;
+constexpr int kXaXP = kXaK + 8;  // x pitch (halves): 144-B rows, A fragments hit bank 4g + c/2
+template <int NC>
+struct XaCfg {
+  static constexpr int AP = NC + 8;  // A pitch (floats): B fragments (k = c, n = g) hit bank 8c + g
+  static constexpr int XBytes = kXaRows * kXaXP * 2, ABytes = kXaK * AP * 4;
+  static constexpr int Smem = kXaStages * (XBytes + ABytes);
+};
+
+__device__ __forceinline__ void xa_cp16(void* dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_xa() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_xa() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t to_tf32(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Requires K % 8 == 0, R % 4 == 0, R <= NC, x and A 16-byte aligned (whole 16-B copies).
+template <int NC>
+__global__ void __launch_bounds__(kXaThreads) lora_xa_tiled_kernel(const __half* x, const float* A, float* t, int M,
+                                                                  int K, int R) {
+  using C = XaCfg<NC>;
+  extern __shared__ __align__(16) uint8_t xa_smem[];
+  auto xs = reinterpret_cast<__half(*)[kXaRows][kXaXP]>(xa_smem);                       // [stage][row][k]
+  auto as = reinterpret_cast<float(*)[kXaK][C::AP]>(xa_smem + kXaStages * C::XBytes);  // [stage][k][col]
   pdl_trigger();
   pdl_wait();
   const int m0 = blockIdx.x * kXaRows;
-  const int tid = threadIdx.x, row = tid >> 3, cgp = tid & 7;
-  float xr[kXaXPer], ar[kXaAPer];
-  auto gload = [&](int k0) {
-#pragma unroll
-    for (int u = 0; u < kXaXPer; ++u) {
-      const int i = tid + 256 * u, r = i / kXaK, k = k0 + (i - r * kXaK), m = m0 + r;
-      xr[u] = (m < M && k < K) ? __half2float(x[(size_t)m * K + k]) : 0.f;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int rg = warp & 1, kq = warp >> 1;
+  const int nchunks = (K + kXaK - 1) / kXaK;
+  auto issue = [&](int ch) {
+    const int st = ch % kXaStages, k0 = ch * kXaK;
+    {  // x: 32 rows x 8 pieces of 8 k, one copy per thread
+      const int r = tid >> 3, q = tid & 7, m = m0 + r, k = k0 + 8 * q;
+      const bool ok = m < M && k < K;
+      xa_cp16(&xs[st][r][8 * q], ok ? x + (size_t)m * K + k : x, ok);
     }
+    constexpr int kSeg = NC / 4;  // 16-B pieces of an A row
 #pragma unroll
-    for (int u = 0; u < kXaAPer; ++u) {
-      const int i = tid + 256 * u, kk = i / kXaCols, j = i - kk * kXaCols, k = k0 + kk;
-      ar[u] = (k < K && j < R) ? A[(size_t)k * R + j] : 0.f;
+    for (int i = tid; i < kXaK * kSeg; i += kXaThreads) {
+      const int kk = i / kSeg, j = 4 * (i - kk * kSeg), k = k0 + kk;
+      const bool ok = k < K && j < R;
+      xa_cp16(&as[st][kk][j], ok ? A + (size_t)k * R + j : A, ok);
     }
   };
-  float acc[kXaCols / 8];
 #pragma unroll
-  for (int i = 0; i < kXaCols / 8; ++i) acc[i] = 0.f;
-  gload(0);
-  for (int k0 = 0; k0 < K; k0 += kXaK) {
-#pragma unroll
-    for (int u = 0; u < kXaXPer; ++u) {
-      const int i = tid + 256 * u, r = i / kXaK;
-      xs[r][i - r * kXaK] = xr[u];
-    }
-#pragma unroll
-    for (int u = 0; u < kXaAPer; ++u) {
-      const int i = tid + 256 * u, kk = i / kXaCols;
-      as[kk][i - kk * kXaCols] = ar[u];
-    }
-    __syncthreads();
-    if (k0 + kXaK < K) gload(k0 + kXaK);
-#pragma unroll 8
-    for (int kk = 0; kk < kXaK; ++kk) {
-      const float xv = xs[row][kk];
-#pragma unroll
-      for (int i = 0; i < kXaCols / 8; ++i) acc[i] = fmaf(xv, as[kk][cgp + 8 * i], acc[i]);
-    }
-    __syncthreads();
+  for (int s = 0; s < kXaStages - 1; ++s) {
+    if (s < nchunks) issue(s);
+    cp_async_commit_xa();
   }
-  const int m = m0 + row;
+  float tot[NC / 8][4];
 #pragma unroll
-  for (int i = 0; i < kXaCols / 8; ++i) {
-    const int j = cgp + 8 * i;
-    if (m < M && j < R) t[(size_t)m * R + j] = acc[i];
+  for (int nt = 0; nt < NC / 8; ++nt) tot[nt][0] = tot[nt][1] = tot[nt][2] = tot[nt][3] = 0.f;
+  const int r0 = 16 * rg + g;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait_xa<kXaStages - 2>();  // this thread's copies of chunk ch have landed
+    __syncthreads();                    // everyone's; and chunk ch - 1's stage is free again
+    if (ch + kXaStages - 1 < nchunks) issue(ch + kXaStages - 1);
+    cp_async_commit_xa();  // empty groups keep the count uniform
+    const int st = ch % kXaStages;
+    uint32_t af[2][4];  // this warp's two 8-k steps of the chunk
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int kb = 8 * (2 * kq + q);
+      af[q][0] = __float_as_uint(__half2float(xs[st][r0][kb + c]));
+      af[q][1] = __float_as_uint(__half2float(xs[st][r0 + 8][kb + c]));
+      af[q][2] = __float_as_uint(__half2float(xs[st][r0][kb + c + 4]));
+      af[q][3] = __float_as_uint(__half2float(xs[st][r0 + 8][kb + c + 4]));
+    }
+#pragma unroll
+    for (int nt = 0; nt < NC / 8; ++nt) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int kb = 8 * (2 * kq + q);
+        const float v0 = as[st][kb + c][8 * nt + g], v1 = as[st][kb + c + 4][8 * nt + g];
+        const uint32_t b0 = to_tf32(v0), b1 = to_tf32(v1);
+        mma_tf32(d, af[q], b0, b1);
+        mma_tf32(d, af[q], to_tf32(v0 - __uint_as_float(b0)), to_tf32(v1 - __uint_as_float(b1)));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tot[nt][e] += d[e];
+    }
   }
+  cp_async_wait_xa<0>();
+  __syncthreads();  // all fragment reads done: the A ring is reused for the quarters' sums
+  float* red = reinterpret_cast<float*>(as);  // [quarter 1..3][row group][nt][e][lane]
+  auto ridx = [&](int qq, int nt, int e) { return ((((qq - 1) * 2 + rg) * (NC / 8) + nt) * 4 + e) * 32 + lane; };
+  if (kq > 0) {
+#pragma unroll
+    for (int nt = 0; nt < NC / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[ridx(kq, nt, e)] = tot[nt][e];
+  }
+  __syncthreads();
+  if (kq > 0) return;
+#pragma unroll
+  for (int nt = 0; nt < NC / 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) tot[nt][e] = ((tot[nt][e] + red[ridx(1, nt, e)]) + red[ridx(2, nt, e)]) + red[ridx(3, nt, e)];
+  // C fragment: (row g, cols 2c, 2c + 1) and (row g + 8, same cols) of each 8-column tile
+  const int ra = m0 + r0, rb = ra + 8;
+#pragma unroll
+  for (int nt = 0; nt < NC / 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int j = 8 * nt + 2 * c + e;
+      if (j < R) {
+        if (ra < M) t[(size_t)ra * R + j] = tot[nt][e];
+        if (rb < M) t[(size_t)rb * R + j] = tot[nt][2 + e];
+      }
+    }
 }
 }  // namespace orch
 
@@ -461,11 +537,28 @@ extern "C" int orch_lora_xa(const void* x, const float* a, float* t, uint32_t M,
                             void* stream) {
   if (M == 0 || R == 0) return ORCH_OK;
   ORCH_REQUIRE(x && a && t && K > 0, "lora_xa: bad arguments");
-  if (M >= 256 && R <= (uint32_t)orch::kXaCols)  // many rows: A staged once per 32 rows
-    ORCH_CUDA(orch::launch_k(orch::lora_xa_tiled_kernel, dim3((M + orch::kXaRows - 1) / orch::kXaRows), dim3(256), 0,
-                             as_stream(stream), dim3(0, 0, 0), (const __half*)x, a, t, (int)M, (int)K, (int)R));
-  else
+  const bool tiled = M >= 256 && R <= 64 && R % 4 == 0 && K % 8 == 0 && ((uintptr_t)x & 15) == 0 &&
+                     ((uintptr_t)a & 15) == 0;  // many rows, whole 16-B copies
+  if (tiled) {
+    static bool attr_done[64] = {};
+    const int dev = device_index();
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      ORCH_CUDA(cudaFuncSetAttribute(orch::lora_xa_tiled_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     orch::XaCfg<32>::Smem));
+      ORCH_CUDA(cudaFuncSetAttribute(orch::lora_xa_tiled_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     orch::XaCfg<64>::Smem));
+      attr_done[dev] = true;
+    }
+    const dim3 grid((M + orch::kXaRows - 1) / orch::kXaRows);
+    if (R <= 32)
+      ORCH_CUDA(orch::launch_k(orch::lora_xa_tiled_kernel<32>, grid, dim3(orch::kXaThreads), orch::XaCfg<32>::Smem,
+                               as_stream(stream), dim3(0, 0, 0), (const __half*)x, a, t, (int)M, (int)K, (int)R));
+    else
+      ORCH_CUDA(orch::launch_k(orch::lora_xa_tiled_kernel<64>, grid, dim3(orch::kXaThreads), orch::XaCfg<64>::Smem,
+                               as_stream(stream), dim3(0, 0, 0), (const __half*)x, a, t, (int)M, (int)K, (int)R));
+  } else {
     ORCH_CUDA(orch::launch_k(orch::lora_xa_kernel, dim3(M), dim3(256), 0, as_stream(stream), dim3(0, 0, 0),
                              (const __half*)x, a, t, (int)K, (int)R));
+  }
   return check_launch("lora_xa");
 }

@@ -304,11 +304,13 @@ def test_attention_decode(M, L, hd):
         assert rel_err(o[m].reshape(nh, hd), ref) <= 1e-2
 
 
-@pytest.mark.parametrize("M,K,R", [(5, 4096, 48), (300, 4096, 48), (4096, 4096, 48), (1000, 96, 16), (4096, 512, 80)])
+@pytest.mark.parametrize("M,K,R", [(5, 4096, 48), (300, 4096, 48), (4096, 4096, 48), (1000, 96, 16), (4096, 512, 80),
+                                   (4096, 4096, 32), (257, 11008, 32), (512, 4096, 30)])
 def test_lora_xa(M, K, R):
-    """t = x.A (the first LoRA factor, orchard/model.py:60-76): fp16 x, fp32 A, fp32 t. Small M
-    takes the one-row-per-CTA kernel, M >= 256 with R <= 64 the tiled one; both are fp32 dot
-    products, so max|gpu - ref| / max|ref| <= 1e-5 against fp32 NumPy."""
+    """t = x.A (the first LoRA factor, orchard/model.py:60-76): fp16 x, fp32 A, fp32 t. Small M,
+    R > 64 or R % 4 != 0 take the one-row-per-CTA fp32 kernel; M >= 256 otherwise the tiled
+    tensor-core one (TF32 with A split in two terms, each 8-k step added in fp32, 32 or 64
+    columns). Both are fp32-accurate: max|gpu - ref| / max|ref| <= 1e-5 against fp32 NumPy."""
     g = np.random.default_rng([31, M, K, R])
     x = g.standard_normal((M, K), dtype=np.float32).astype(np.float16)
     a = (g.standard_normal((K, R), dtype=np.float32) * 0.01).astype(np.float32)
