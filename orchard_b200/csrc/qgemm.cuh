@@ -163,6 +163,11 @@ struct LoraGlobal {  // the LoRA term from the operands in global memory
     constexpr int R = EPI == EPI_QKV ? 3 : (EPI == EPI_SWIGLU ? 2 : 1);
     return lora_delta_r<R>(a, n, reg, col, width);
   }
+  // columns col and col + 1 (a RoPE pair)
+  __device__ __forceinline__ void pair(int n, int reg, int col, int width, float& d0, float& d1) const {
+    d0 = (*this)(n, reg, col, width);
+    d1 = (*this)(n, reg, col + 1, width);
+  }
 };
 
 // STORE / RESID: the value of output (n, row idx) before it is stored or added.
@@ -200,8 +205,10 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
     const int rr = idx - region * a.H;
     const int head = rr / a.hd, d = rr - head * a.hd;
     if (a.lora_t != nullptr) {
-      v0 += lora(n, region, rr, a.H);
-      v1 += lora(n, region, rr + 1, a.H);
+      float d0, d1;
+      lora.pair(n, region, rr, a.H, d0, d1);
+      v0 += d0;
+      v1 += d1;
     }
     const int p = a.pos[n];
     if (p < 0 || p >= a.max_seq || p >= a.max_pos) {

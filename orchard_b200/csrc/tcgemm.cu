@@ -89,6 +89,35 @@ struct LoraSmem {
     for (int q = 0; q < r; ++q) v = fmaf(t[q], b[q * cw], v);
     return v;
   }
+  // Columns col and col + 1 of a RoPE pair (col - c0 even: 8-byte aligned in bs): t[n] is
+  // read once for both and B as float2, a third of the shared-memory wavefronts of two calls
+  // (a warp's t row is one broadcast address; its B pairs are 256 contiguous bytes).
+  __device__ __forceinline__ void pair(int n, int reg, int col, int width, float& d0, float& d1) const {
+    const float* t = ts + ((size_t)(reg - reg0) * Mp + n) * r;
+    const float* b = bs + (size_t)(reg - reg0) * r * cw + (col - c0);
+    float v0 = 0.f, v1 = 0.f;
+    if ((r & 3) == 0) {  // t rows 16-byte aligned
+      for (int q = 0; q < r; q += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(t + q);
+        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 bb = *reinterpret_cast<const float2*>(b + (q + u) * cw);
+          v0 = fmaf(tv[u], bb.x, v0);
+          v1 = fmaf(tv[u], bb.y, v1);
+        }
+      }
+    } else {
+      for (int q = 0; q < r; ++q) {
+        const float tq = t[q];
+        const float2 bb = *reinterpret_cast<const float2*>(b + q * cw);
+        v0 = fmaf(tq, bb.x, v0);
+        v1 = fmaf(tq, bb.y, v1);
+      }
+    }
+    d0 = v0;
+    d1 = v1;
+  }
 };
 
 // LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 64 bytes.
@@ -356,11 +385,13 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     const int cw = EPI == EPI_SWIGLU ? kTcRows / 2 : kTcRows;
     const int width = EPI == EPI_QKV ? a.H : (EPI == EPI_SWIGLU ? a.N >> 1 : a.N);
     const int r = a.lora_r;
-    const int recv_floats = epi_recv_floats<kTcRows>(mcount);
-    const size_t need = (size_t)nreg * r * (Mp + cw) * sizeof(float);
-    if ((EPI != EPI_QKV || c0 + kTcRows <= a.H) && (size_t)recv_floats * 4 + need <= (size_t)C::OffBar) {
-      float* ts = recv + recv_floats;
-      float* bs = ts + (size_t)nreg * Mp * r;
+    // both staged arrays start on 16-byte boundaries (the pair reads above)
+    const int ts_off = (epi_recv_floats<kTcRows>(mcount) + 3) & ~3;
+    const int bs_off = ts_off + ((nreg * Mp * r + 3) & ~3);
+    const size_t need = (size_t)(bs_off + nreg * r * cw) * sizeof(float);
+    if ((EPI != EPI_QKV || c0 + kTcRows <= a.H) && need <= (size_t)C::OffBar) {
+      float* ts = recv + ts_off;
+      float* bs = recv + bs_off;
       for (int i = tid; i < nreg * Mp * r; i += kTcThreads2) {
         const int g = i / (Mp * r), rem = i - g * Mp * r, n = rem / r, q = rem - n * r;
         ts[i] = n < mcount ? a.lora_t[((size_t)n * RR + reg0 + g) * r + q] : 0.f;

@@ -103,13 +103,15 @@ def test_tc_fused_epilogues_match_mma_path(M):
         assert rel_err(a, b) <= 5e-3
 
 
-def test_tc_fused_epilogues_with_lora_prefill_rows():
-    """Prefill-sized batch (a full 256-row tile and a partial one) with rank-16 LoRA terms on
+@pytest.mark.parametrize("r", [16, 6])
+def test_tc_fused_epilogues_with_lora_prefill_rows(r):
+    """Prefill-sized batch (a full 256-row tile and a partial one) with rank-r LoRA terms on
     the three fused entry points: the tensor-core kernel (LoRA operands staged in shared
-    memory after the K loop) against the mma.sync kernel (LoRA operands read from global
-    memory); same kernel-to-kernel tolerance as above."""
-    M, H, F, nh, hd, max_seq, r = 300, 4096, 11008, 32, 128, 512, 16
-    g = np.random.default_rng([10, M])
+    memory after the K loop; RoPE pairs read t once, as float4 when r % 4 == 0) against the
+    mma.sync kernel (LoRA operands read from global memory); same kernel-to-kernel tolerance
+    as above."""
+    M, H, F, nh, hd, max_seq = 300, 4096, 11008, 32, 128, 512
+    g = np.random.default_rng([10, M, r])
     pq, sq, _ = weights(3 * H, H)
     p13, s13, _ = weights(2 * F, H)
     p2, s2, _ = weights(H, F)
