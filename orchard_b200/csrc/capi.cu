@@ -316,6 +316,7 @@ static int qkv_rope(const void* wqkv, const void* sqkv, bool tiled, const void* 
   ORCH_REQUIRE(num_heads > 0 && H % num_heads == 0, "q4_qkv_rope: H must be a multiple of num_heads");
   const uint32_t hd = H / num_heads;
   ORCH_REQUIRE(hd % 2 == 0, "q4_qkv_rope: head_dim must be even");
+  ORCH_REQUIRE(H < 65536, "q4_qkv_rope: H must be below 65536");
   ORCH_REQUIRE(max_seq > 0 && max_pos > 0, "q4_qkv_rope: empty cache");
   QArgs a = base_args(wqkv, sqkv, x, ORCH_F16, M, K, 3 * H);
   a.tiled = tiled;
@@ -323,6 +324,7 @@ static int qkv_rope(const void* wqkv, const void* sqkv, bool tiled, const void* 
   a.H = (int)H;
   a.nh = (int)num_heads;
   a.hd = (int)hd;
+  a.hd_magic = (uint32_t)((0x100000000ull + hd - 1) / hd);
   a.max_seq = (int)max_seq;
   a.max_pos = (int)max_pos;
   a.pos = pos;

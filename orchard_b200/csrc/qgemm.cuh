@@ -42,6 +42,7 @@ struct QArgs {
   int ldo;
   // QKV + RoPE + KV append
   int H, nh, hd, max_seq, max_pos;
+  uint32_t hd_magic;  // ceil(2^32 / hd): rr / hd = umulhi(rr, hd_magic) for rr, hd < 2^16
   const int* pos;
   const int* slots;   // cache slot of each row; null: row index (slot0 + local row)
   int slot0;          // with null slots, the first row's index (row blocks advance it)
@@ -201,9 +202,13 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
     static_cast<__half*>(a.out)[(size_t)n * F + idx] = __float2half_rn(si * v1);
   } else {  // EPI_QKV
     const int half_hd = a.hd >> 1;
-    const int region = idx / a.H;
+    const int region = idx >= a.H ? (idx >= 2 * a.H ? 2 : 1) : 0;  // idx < 3H (the caller's check)
     const int rr = idx - region * a.H;
-    const int head = rr / a.hd, d = rr - head * a.hd;
+    // division by an invariant integer as a multiply-high (Granlund & Montgomery): with
+    // m = ceil(2^32 / hd) = (2^32 + e) / hd, 0 <= e < hd, the error rr e / (hd 2^32) stays
+    // below 1 / hd for rr < 2^16, so the floor is exact
+    const int head = (int)__umulhi((uint32_t)rr, a.hd_magic);
+    const int d = rr - head * a.hd;
     if (a.lora_t != nullptr) {
       float d0, d1;
       lora.pair(n, region, rr, a.H, d0, d1);

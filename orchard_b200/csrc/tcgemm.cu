@@ -80,13 +80,13 @@ struct TcCfg {
 // the K loop instead of 2r global loads per output. Same FMA order as lora_delta_r.
 struct LoraSmem {
   const float* ts;  // [region][Mp][r]
-  const float* bs;  // [region][r][cw]
-  int reg0, c0, cw, r, Mp;
+  const float* bs;  // [region][r][bp]: columns c0.. of B, row pitch bp
+  int reg0, c0, bp, r, Mp;
   __device__ __forceinline__ float operator()(int n, int reg, int col, int width) const {
     const float* t = ts + ((size_t)(reg - reg0) * Mp + n) * r;
-    const float* b = bs + (size_t)(reg - reg0) * r * cw + (col - c0);
+    const float* b = bs + (size_t)(reg - reg0) * r * bp + (col - c0);
     float v = 0.f;
-    for (int q = 0; q < r; ++q) v = fmaf(t[q], b[q * cw], v);
+    for (int q = 0; q < r; ++q) v = fmaf(t[q], b[q * bp], v);
     return v;
   }
   // Columns col and col + 1 of a RoPE pair (col - c0 even: 8-byte aligned in bs): t[n] is
@@ -94,7 +94,7 @@ struct LoraSmem {
   // (a warp's t row is one broadcast address; its B pairs are 256 contiguous bytes).
   __device__ __forceinline__ void pair(int n, int reg, int col, int width, float& d0, float& d1) const {
     const float* t = ts + ((size_t)(reg - reg0) * Mp + n) * r;
-    const float* b = bs + (size_t)(reg - reg0) * r * cw + (col - c0);
+    const float* b = bs + (size_t)(reg - reg0) * r * bp + (col - c0);
     float v0 = 0.f, v1 = 0.f;
     if ((r & 3) == 0) {  // t rows 16-byte aligned
       for (int q = 0; q < r; q += 4) {
@@ -102,7 +102,7 @@ struct LoraSmem {
         const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const float2 bb = *reinterpret_cast<const float2*>(b + (q + u) * cw);
+          const float2 bb = *reinterpret_cast<const float2*>(b + (q + u) * bp);
           v0 = fmaf(tv[u], bb.x, v0);
           v1 = fmaf(tv[u], bb.y, v1);
         }
@@ -110,7 +110,7 @@ struct LoraSmem {
     } else {
       for (int q = 0; q < r; ++q) {
         const float tq = t[q];
-        const float2 bb = *reinterpret_cast<const float2*>(b + q * cw);
+        const float2 bb = *reinterpret_cast<const float2*>(b + q * bp);
         v0 = fmaf(tq, bb.x, v0);
         v1 = fmaf(tq, bb.y, v1);
       }
@@ -122,6 +122,68 @@ struct LoraSmem {
 
 // LAY 0: weights in the reference layout, read by 2-D TMA boxes of 128 rows x 64 bytes.
 // LAY 1: weights in the tiled layout (qgemm.cuh), read by contiguous 8 KB bulk copies.
+// LoRA term of a prefill QKV tile whose K range this CTA holds alone, added into its receive
+// buffer before the epilogue: D[n][c] = sum_q t[n][q] B[q][c] for tokens n < Mp and the
+// tile's 128 columns (column c is item row c / 2, pair element c % 2). mma.sync m16n8k8 with
+// both operands split into two TF32 terms and the three products big.big + big.small +
+// small.big (the dropped small.small is below 2^-22 of the product); k zero-padded to a
+// multiple of 8. A warp takes units of 16 tokens x 64 columns: the t fragments of up to 32 k
+// stay in registers across the unit's eight 16 x 8 output tiles. B is staged with a row pitch
+// bp = 8 (mod 32) floats, so a fragment load (k = c, column g) touches 32 distinct banks.
+__device__ __forceinline__ void lora_qkv_tile_into_recv(float* recv, const float* ts, const float* bs, int bp, int Mp,
+                                                        int r, int warp, int nwarps, int lane) {
+  constexpr int IRL = kTcRows / 2, NTU = kTcRows / 16;  // output tiles of 8 columns per unit
+  const int g = lane >> 2, c = lane & 3;
+  const int units = ((Mp + 15) / 16) * 2;
+  for (int u = warp; u < units; u += nwarps) {
+    const int m0 = (u >> 1) * 16, cb = (u & 1) * (kTcRows / 2);
+    for (int kc = 0; kc < r; kc += 32) {
+      uint32_t tb[4][4], tl[4][4];  // t fragments of k steps kc + 8s: big, small terms
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        const int qa = kc + 8 * st + c, qb = qa + 4;
+        const float fa[4] = {m0 + g < Mp && qa < r ? ts[(m0 + g) * r + qa] : 0.f,
+                             m0 + g + 8 < Mp && qa < r ? ts[(m0 + g + 8) * r + qa] : 0.f,
+                             m0 + g < Mp && qb < r ? ts[(m0 + g) * r + qb] : 0.f,
+                             m0 + g + 8 < Mp && qb < r ? ts[(m0 + g + 8) * r + qb] : 0.f};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          tb[st][i] = to_tf32(fa[i]);
+          tl[st][i] = to_tf32(fa[i] - __uint_as_float(tb[st][i]));
+        }
+      }
+#pragma unroll 2
+      for (int j = 0; j < NTU; ++j) {
+        const int n0 = cb + 8 * j;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          if (kc + 8 * st < r) {
+            const int qa = kc + 8 * st + c, qb = qa + 4;
+            const float fb0 = qa < r ? bs[qa * bp + n0 + g] : 0.f;
+            const float fb1 = qb < r ? bs[qb * bp + n0 + g] : 0.f;
+            const uint32_t bb0 = to_tf32(fb0), bb1 = to_tf32(fb1);
+            mma_tf32(d, tl[st], bb0, bb1);  // small terms first
+            mma_tf32(d, tb[st], to_tf32(fb0 - __uint_as_float(bb0)), to_tf32(fb1 - __uint_as_float(bb1)));
+            mma_tf32(d, tb[st], bb0, bb1);
+          }
+        }
+        // d[0], d[1]: token m0 + g, columns n0 + 2c, n0 + 2c + 1 (item n0 / 2 + c, elements 0,
+        // 1); d[2], d[3]: token m0 + g + 8
+        const int irl = (n0 >> 1) + c;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n = m0 + g + 8 * h;
+          if (n < Mp) {
+            recv[(size_t)n * (IRL + 1) + irl] += d[2 * h];
+            recv[((size_t)Mp + n) * (IRL + 1) + irl] += d[2 * h + 1];
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int EPI, int NTILE, int LAY>
 __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
@@ -388,7 +450,8 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     // both staged arrays start on 16-byte boundaries (the pair reads above)
     const int ts_off = (epi_recv_floats<kTcRows>(mcount) + 3) & ~3;
     const int bs_off = ts_off + ((nreg * Mp * r + 3) & ~3);
-    const size_t need = (size_t)(bs_off + nreg * r * cw) * sizeof(float);
+    const int bp = cw + 8;  // staged B pitch (floats; 8 mod 32 for cw = 128)
+    const size_t need = (size_t)(bs_off + nreg * r * bp) * sizeof(float);
     if ((EPI != EPI_QKV || c0 + kTcRows <= a.H) && need <= (size_t)C::OffBar) {
       float* ts = recv + ts_off;
       float* bs = recv + bs_off;
@@ -397,11 +460,19 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
         ts[i] = n < mcount ? a.lora_t[((size_t)n * RR + reg0 + g) * r + q] : 0.f;
       }
       for (int i = tid; i < nreg * r * cw; i += kTcThreads2) {
-        const int g = i / (r * cw), rem = i - g * r * cw, q = rem / cw, col = c0 + (rem - q * cw);
-        bs[i] = col < width ? a.lora_b[((size_t)(reg0 + g) * r + q) * width + col] : 0.f;
+        const int g = i / (r * cw), rem = i - g * r * cw, q = rem / cw, cl = rem - q * cw, col = c0 + cl;
+        bs[(g * r + q) * bp + cl] = col < width ? a.lora_b[((size_t)(reg0 + g) * r + q) * width + col] : 0.f;
+      }
+      if (EPI == EPI_QKV && KS == 1) {
+        // the receive buffer holds this CTA's whole sums: add the LoRA term there
+        __syncthreads();
+        lora_qkv_tile_into_recv(recv, ts, bs, bp, Mp, r, warp, kTcThreads2 / 32, lane);
+        a.lora_t = nullptr;
+        qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0);
+        return;
       }
       // qgemm_finish's cluster barrier orders these stores before the epilogue reads them
-      qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0, LoraSmem{ts, bs, reg0, c0, cw, r, Mp});
+      qgemm_finish<W_Q4, EPI, kTcRows>(a, recv, KS, ks, R0, LoraSmem{ts, bs, reg0, c0, bp, r, Mp});
       return;
     }
   }
