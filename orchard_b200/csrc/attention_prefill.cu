@@ -13,7 +13,11 @@
 //  * O += P V with P split into fp16 hi + lo terms (P - hi rounded to fp16), so the
 //    probabilities keep ~22 bits and the result stays at fp32-level accuracy.
 // Keys past the unit's last position are zero-filled in shared memory (never read from the
-// cache), so stale cache contents cannot reach the output.
+// cache), so stale cache contents cannot reach the output. K and V blocks are copied row-major
+// with cp.async into a double buffer (the next block in flight while one is multiplied); the
+// MMA operands come from ldmatrix (K rows as the B operand of Q K^T, V rows transposed by
+// ldmatrix.trans as the B operand of P V), with a row pitch of 136 halves so the eight rows
+// of each 8 x 8 matrix fall in distinct banks.
 #include "orch_common.cuh"
 
 namespace orch {
@@ -23,9 +27,9 @@ namespace {
 constexpr int kPfRows = 64;            // query rows per CTA: 4 warps x 16
 constexpr int kPfKeys = 64;            // keys per block
 constexpr int kPfHD = 128;             // head dim
-constexpr int kPfQP = kPfHD + 8;       // Q / K smem row pitch (halves): conflict-free fragment loads
-constexpr int kPfVP = kPfKeys + 8;     // transposed-V smem row pitch (halves)
-constexpr int kPfSmem = (kPfRows * kPfQP + kPfKeys * kPfQP + kPfHD * kPfVP) * 2;
+constexpr int kPfP = kPfHD + 8;        // Q / K / V smem row pitch (halves): 272 B, 16-byte aligned
+constexpr int kPfTile = kPfKeys * kPfP;  // one K or V block (halves)
+constexpr int kPfSmem = 4 * kPfTile * 2;  // double buffer of K and V blocks; Q staged in buffer 1
 
 struct PfArgs {
   const __half* q;
@@ -40,11 +44,25 @@ struct PfArgs {
 __device__ __forceinline__ uint32_t ld_h2(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) { return h2_bits(__floats2half2_rn(lo, hi)); }
 
+__device__ __forceinline__ void pf_cp16(const void* dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(const __half* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+__device__ __forceinline__ void ldsm_x4_t(const __half* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const PfArgs a) {
   extern __shared__ __align__(16) uint8_t pf_smem[];
-  __half* qs = reinterpret_cast<__half*>(pf_smem);
-  __half* ks = qs + kPfRows * kPfQP;
-  __half* vt = ks + kPfKeys * kPfQP;  // V block transposed: [dim][key]
+  __half* kbuf = reinterpret_cast<__half*>(pf_smem);  // [buffer][K, V][key][dim], pitch kPfP
   pdl_trigger();
   pdl_wait();
 
@@ -58,68 +76,78 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PfArgs a) {
   }
   const int H = a.nh * kPfHD;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const size_t base = ((size_t)slot * a.nh + h) * a.max_seq * kPfHD;
+  const int nkb = plast / kPfKeys + 1;
 
+  // K and V rows of block kb into buffer kb & 1 (keys past plast zero-filled, not read)
+  auto issue = [&](int kb) {
+    __half* kd = kbuf + (kb & 1) * 2 * kPfTile;
+    __half* vd = kd + kPfTile;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = tid + 128 * j, r = i >> 4, d8 = (i & 15) * 8, key = kb * kPfKeys + r;
+      const bool ok = key <= plast;
+      const size_t off = ok ? base + (size_t)key * kPfHD + d8 : 0;
+      pf_cp16(kd + r * kPfP + d8, a.kc + off, ok);
+      pf_cp16(vd + r * kPfP + d8, a.vc + off, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue(0);
+
+  // Q rows through buffer 1's K area, then into registers (A fragments of 16 rows x 16 dims)
+  __half* qs = kbuf + 2 * kPfTile;
   for (int i = tid; i < kPfRows * (kPfHD / 8); i += 128) {
     const int r = i >> 4, d8 = (i & 15) * 8;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (r < n) v = *reinterpret_cast<const uint4*>(a.q + (size_t)(row0 + r) * H + h * kPfHD + d8);
-    *reinterpret_cast<uint4*>(qs + r * kPfQP + d8) = v;
+    *reinterpret_cast<uint4*>(qs + r * kPfP + d8) = v;
   }
   __syncthreads();
   const int qr = warp * 16 + g;  // this thread's rows: qr and qr + 8
   uint32_t qa[kPfHD / 16][4];
 #pragma unroll
   for (int kk = 0; kk < kPfHD / 16; ++kk) {
-    qa[kk][0] = ld_h2(qs + qr * kPfQP + 16 * kk + 2 * c);
-    qa[kk][1] = ld_h2(qs + (qr + 8) * kPfQP + 16 * kk + 2 * c);
-    qa[kk][2] = ld_h2(qs + qr * kPfQP + 16 * kk + 8 + 2 * c);
-    qa[kk][3] = ld_h2(qs + (qr + 8) * kPfQP + 16 * kk + 8 + 2 * c);
+    qa[kk][0] = ld_h2(qs + qr * kPfP + 16 * kk + 2 * c);
+    qa[kk][1] = ld_h2(qs + (qr + 8) * kPfP + 16 * kk + 2 * c);
+    qa[kk][2] = ld_h2(qs + qr * kPfP + 16 * kk + 8 + 2 * c);
+    qa[kk][3] = ld_h2(qs + (qr + 8) * kPfP + 16 * kk + 8 + 2 * c);
   }
+  __syncthreads();  // buffer 1 is free for block 1
 
   float o[kPfHD / 8][4];
 #pragma unroll
   for (int d = 0; d < kPfHD / 8; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float scale = rsqrtf((float)kPfHD);
-  const size_t base = ((size_t)slot * a.nh + h) * a.max_seq * kPfHD;
   const int qp0 = p0 + qr, qp1 = p0 + qr + 8;  // positions of the two rows
-  const int nkb = plast / kPfKeys + 1;
+  // ldmatrix row addresses of this lane: matrix lane >> 3, row lane & 7
+  const int lm = lane >> 3, lr = lane & 7;
 
   for (int kb = 0; kb < nkb; ++kb) {
     const int k0 = kb * kPfKeys;
-    __syncthreads();  // the previous block's K and V are no longer read
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {  // 64 keys x 16 chunks of 8 dims, 4 per thread per half
-      uint4 kv[4], vv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = tid + 128 * (4 * half + j), r = i >> 4, d8 = (i & 15) * 8, key = k0 + r;
-        kv[j] = vv[j] = make_uint4(0u, 0u, 0u, 0u);
-        if (key <= plast) {
-          kv[j] = ld_stream16(a.kc + base + (size_t)key * kPfHD + d8);
-          vv[j] = ld_stream16(a.vc + base + (size_t)key * kPfHD + d8);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = tid + 128 * (4 * half + j), r = i >> 4, d8 = (i & 15) * 8;
-        *reinterpret_cast<uint4*>(ks + r * kPfQP + d8) = kv[j];
-        const __half* vh = reinterpret_cast<const __half*>(&vv[j]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vt[(d8 + e) * kPfVP + r] = vh[e];
-      }
+    if (kb + 1 < nkb) {
+      issue(kb + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    __syncthreads();
+    __syncthreads();  // block kb's rows from every thread's copies
+    const __half* ks = kbuf + (kb & 1) * 2 * kPfTile;
+    const __half* vs = ks + kPfTile;
 
-    // S = Q K^T for this warp's 16 rows x 64 keys (8 tiles of 8 keys)
+    // S = Q K^T for this warp's 16 rows x 64 keys (8 tiles of 8 keys). ldmatrix x4 per key
+    // tile and dim pair kk, kk + 1: matrices (dims 16kk, +8, 16kk + 16, +24) of keys 8t..8t+7
     float sc[kPfKeys / 8][4];
 #pragma unroll
     for (int t = 0; t < kPfKeys / 8; ++t) {
       sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < kPfHD / 16; ++kk) {
-        const __half* kr = ks + (8 * t + g) * kPfQP + 16 * kk + 2 * c;
-        mma_16816(sc[t], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], ld_h2(kr), ld_h2(kr + 8));
+      for (int kk = 0; kk < kPfHD / 16; kk += 2) {
+        uint32_t b[4];
+        ldsm_x4(ks + (8 * t + lr) * kPfP + 16 * kk + 8 * lm, b);
+        mma_16816(sc[t], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b[0], b[1]);
+        mma_16816(sc[t], qa[kk + 1][0], qa[kk + 1][1], qa[kk + 1][2], qa[kk + 1][3], b[2], b[3]);
       }
     }
     // scale, causal mask, running max
@@ -163,7 +191,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PfArgs a) {
       o[d][2] *= al1;
       o[d][3] *= al1;
     }
-    // O += P V: keys 16 j .. 16 j + 15 per k-step; P from the score tiles 2 j, 2 j + 1
+    // O += P V: keys 16 j .. 16 j + 15 per k-step; P from the score tiles 2 j, 2 j + 1. V by
+    // ldmatrix.trans, x4 per dim pair d, d + 1: matrices (keys 16j, 16j + 8) x (dims 8d, 8d + 8)
 #pragma unroll
     for (int j = 0; j < kPfKeys / 16; ++j) {
       const float* s0 = sc[2 * j];
@@ -184,13 +213,16 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const PfArgs a) {
         lo[3] = pack_h2(pv[6] - ph[6], pv[7] - ph[7]);
       }
 #pragma unroll
-      for (int d = 0; d < kPfHD / 8; ++d) {
-        const __half* vr = vt + (8 * d + g) * kPfVP + 16 * j + 2 * c;
-        const uint32_t b0 = ld_h2(vr), b1 = ld_h2(vr + 8);
-        mma_16816(o[d], hi[0], hi[1], hi[2], hi[3], b0, b1);
-        mma_16816(o[d], lo[0], lo[1], lo[2], lo[3], b0, b1);
+      for (int d = 0; d < kPfHD / 8; d += 2) {
+        uint32_t b[4];
+        ldsm_x4_t(vs + (16 * j + 8 * (lm & 1) + lr) * kPfP + 8 * d + 8 * (lm >> 1), b);
+        mma_16816(o[d], hi[0], hi[1], hi[2], hi[3], b[0], b[1]);
+        mma_16816(o[d], lo[0], lo[1], lo[2], lo[3], b[0], b[1]);
+        mma_16816(o[d + 1], hi[0], hi[1], hi[2], hi[3], b[2], b[3]);
+        mma_16816(o[d + 1], lo[0], lo[1], lo[2], lo[3], b[2], b[3]);
       }
     }
+    __syncthreads();  // every warp is done with buffer kb & 1 before block kb + 2 is copied in
   }
 
 #pragma unroll
