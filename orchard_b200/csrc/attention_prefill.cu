@@ -60,7 +60,7 @@ __device__ __forceinline__ void ldsm_x4_t(const __half* p, uint32_t (&r)[4]) {
                : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
 }
 
-__global__ void __launch_bounds__(128) attn_prefill_kernel(const PfArgs a) {
+__global__ void __launch_bounds__(128, 3) attn_prefill_kernel(const PfArgs a) {
   extern __shared__ __align__(16) uint8_t pf_smem[];
   __half* kbuf = reinterpret_cast<__half*>(pf_smem);  // [buffer][K, V][key][dim], pitch kPfP
   pdl_trigger();
