@@ -15,6 +15,8 @@ from __future__ import annotations
 import argparse
 import json
 
+import numpy as np
+
 import torch
 
 from . import _lib
@@ -119,10 +121,35 @@ def time_attn(M: int, L: int, reps: int, nh: int = 32, hd: int = 128, max_seq: i
             "bytes": byts, "cache_copies": n}
 
 
+def time_attn_prefill(seqs: int, L: int, reps: int, nh: int = 32, hd: int = 128, max_seq: int = 640):
+    """Causal prefill attention (orch_attention_prefill) for `seqs` sequences of L tokens at
+    positions 0..L-1: q [seqs*L, nh*hd], K / V caches of `seqs` slots. One copy of the inputs
+    (the kernel is tensor-bound; with 8 x 512 tokens q + K + V = 100 MB)."""
+    from .model import prefill_units
+
+    dev = "cuda"
+    M = seqs * L
+    q = torch.randn((M, nh * hd), device=dev).half()
+    kc = torch.randn((seqs, nh, max_seq, hd), device=dev).half()
+    vc = torch.randn_like(kc)
+    units = torch.from_numpy(prefill_units(np.tile(np.arange(L), seqs), np.repeat(np.arange(seqs), L))).to(dev)
+    out = torch.empty_like(q)
+
+    def run(i):
+        call("orch_attention_prefill", q, kc, vc, units, units.shape[0], out, M, nh, hd, max_seq,
+             torch.cuda.current_stream().cuda_stream)
+
+    us = _graph_time(run, 1, reps)
+    flops = 2 * 2 * seqs * nh * (L * (L + 1) // 2) * hd  # QK^T and PV over the causal pairs
+    return {"kernel": "attention_prefill", "seqs": seqs, "L": L, "us": round(us, 3),
+            "TFLOPs": round(flops / us / 1e6, 1), "flops": flops}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default="all", choices=["q4", "q4t", "q8pc", "attn", "all"])
-    ap.add_argument("--M", default="1,16,64")
+    ap.add_argument("--kernel", default="all", choices=["q4", "q4t", "q8pc", "attn", "attn_prefill", "all"])
+    ap.add_argument("--M", default="1,16,64", help="activation rows (attn_prefill: sequences)")
+    ap.add_argument("--L", type=int, default=512, help="attn_prefill: tokens per sequence")
     ap.add_argument("--shape", default="", help="only this decode shape name (qkv, o, gate_up, down, lm_head)")
     ap.add_argument("--shapes", default="", help="extra GEMM shapes K:N,K:N,... (timed instead of the decode shapes)")
     ap.add_argument("--reps", type=int, default=50)
@@ -143,6 +170,8 @@ def main():
                     print(json.dumps(r), flush=True)
         if a.kernel in ("attn", "all"):
             print(json.dumps(time_attn(M, 577, a.reps)), flush=True)
+        if a.kernel == "attn_prefill":
+            print(json.dumps(time_attn_prefill(M, a.L, a.reps)), flush=True)
 
 
 if __name__ == "__main__":
