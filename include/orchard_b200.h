@@ -158,7 +158,8 @@ int orch_q4_linear_swiglu(const void* w13, const void* s13, const void* x, void*
 /* Q/K/V projection + RoPE + KV-cache append (orchard/model.py:94-124). wqkv: [3H, K] =
  * [Wq; Wk; Wv]. Rotates q and k with cos/sin tables [max_pos, head_dim/2] (fp32) at
  * pos[m]; writes q fp16 [M,H]; appends k, v fp16 to the caches laid out
- * [slots][num_heads][max_seq][head_dim] at slot slots[m] (NULL = m), position pos[m]. */
+ * [slots][num_heads][max_seq][head_dim] at slot slots[m] (NULL = m), position pos[m].
+ * H = num_heads * head_dim must be below 65536 and head_dim even. */
 int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* x, uint32_t M, uint32_t K,
                      uint32_t H, uint32_t num_heads, const int32_t* pos, const int32_t* slots,
                      const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,

@@ -157,6 +157,13 @@ def test_tiled_rejects_bad_arguments():
         call("orch_q4t_gemm", t[8:], x, y, F32, 4096, 256, 2, S())
     with pytest.raises(_lib.OrchardError):
         call("orch_q4t_pack", torch.from_numpy(p).cuda(), torch.from_numpy(s).cuda(), 256, 100, t, S())
+    # H = 512 heads x 128 = 65536: beyond the epilogue's head-index arithmetic (H < 65536);
+    # rejected on the host before any launch, so the small buffers are never touched
+    small = torch.zeros(16, dtype=torch.float32, device="cuda")
+    pos = torch.zeros(2, dtype=torch.int32, device="cuda")
+    with pytest.raises(_lib.OrchardError):
+        call("orch_q4t_qkv_rope", t, x, 2, 4096, 65536, 512, pos, None, small, small, 16, small, small, small, 4,
+             None, None, 0, S())
 
 
 @pytest.mark.parametrize("M", [1, 5, 16, 64, 200])
