@@ -62,3 +62,28 @@ def test_lora_loader_matches_reference_layout(tmp_path, golden_model):
         for name in ("wq", "wv"):
             np.testing.assert_array_equal(per_layer[li][name][0], m.layers[li].lora[name][0])
             np.testing.assert_array_equal(per_layer[li][name][1], m.layers[li].lora[name][1])
+
+
+def test_prefill_units_cover_rows_in_runs():
+    """Work units of the prefill attention kernel: every row exactly once and in order; a
+    unit never spans a change of cache slot or a gap in positions, and holds at most
+    max_rows rows (the kernel's 64-row tile)."""
+    pos, slots = [], []
+    for slot, (start, n) in enumerate([(0, 130), (5, 1), (0, 64), (300, 65), (7, 3)]):
+        pos += list(range(start, start + n))
+        slots += [slot] * n
+    pos[200] += 3  # a gap in positions inside slot 3's run
+    u = model.prefill_units(pos, slots)
+    assert u.dtype == np.int32 and u.shape[1] == 4
+    rows = np.concatenate([np.arange(r0, r0 + n) for r0, n, _, _ in u])
+    np.testing.assert_array_equal(rows, np.arange(len(pos)))
+    for r0, n, slot, p0 in u:
+        assert 1 <= n <= 64
+        assert all(slots[r0 + i] == slot and pos[r0 + i] == p0 + i for i in range(n))
+    # unit starts are exactly the run starts plus every 64th row of a run
+    brk = [0] + [i for i in range(1, len(pos)) if slots[i] != slots[i - 1] or pos[i] != pos[i - 1] + 1]
+    ends = brk[1:] + [len(pos)]
+    expect = [r for a, e in zip(brk, ends) for r in range(a, e, 64)]
+    assert u[:, 0].tolist() == expect
+    assert model.prefill_units([], []).shape == (0, 4)
+    assert model.prefill_units(list(range(10)), [0] * 10, max_rows=4)[:, 1].tolist() == [4, 4, 2]
