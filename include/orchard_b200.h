@@ -53,8 +53,13 @@ int orch_init(int device, const char* resource_path);
 int orch_is_available(void);
 /* MetalBackend::get_device_name (metal_backend.h:16; bindings.cpp:18). */
 int orch_device_name(char* buf, size_t len);
-/* Reads and clears the device-side check word (nonzero after a kernel rejected an input,
- * e.g. an out-of-range token id). */
+/* Reads and clears the device-side check flags: nonzero after a kernel rejected an input and
+ * skipped the work it covers. Bits: 1 a Q/K/V row's position outside the cache or RoPE
+ * table (that row's q/k/v not written); 2 an attention row's position outside the cache
+ * or a bad prefill unit (its output not written); 4 an embedding id outside the vocabulary
+ * (zero row); 8 a cache slot outside [0, num_slots) (no cache read or write for that row);
+ * 256 a tensor-core GEMM's bounded wait ran out. Covers the allocation-free attention
+ * entry point's flags as well. */
 int orch_device_check(uint32_t* flags_out, void* stream);
 
 /* ---- buffers (metal_backend.h:19-22; tensor.cpp:17-72) -------------------------------- */
@@ -158,13 +163,15 @@ int orch_q4_linear_swiglu(const void* w13, const void* s13, const void* x, void*
 /* Q/K/V projection + RoPE + KV-cache append (orchard/model.py:94-124). wqkv: [3H, K] =
  * [Wq; Wk; Wv]. Rotates q and k with cos/sin tables [max_pos, head_dim/2] (fp32) at
  * pos[m]; writes q fp16 [M,H]; appends k, v fp16 to the caches laid out
- * [slots][num_heads][max_seq][head_dim] at slot slots[m] (NULL = m), position pos[m].
- * H = num_heads * head_dim must be below 65536 and head_dim even. */
+ * [num_slots][num_heads][max_seq][head_dim] at slot slots[m] (NULL = m), position pos[m];
+ * a row whose slot is outside [0, num_slots) or whose position is outside the cache writes
+ * nothing and sets a device check bit (8 / 1). H = num_heads * head_dim must be below 65536
+ * and head_dim even. */
 int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* x, uint32_t M, uint32_t K,
                      uint32_t H, uint32_t num_heads, const int32_t* pos, const int32_t* slots,
                      const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
-                     void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
-                     const float* lora_b, uint32_t lora_r, void* stream);
+                     void* k_cache, void* v_cache, uint32_t max_seq, uint32_t num_slots,
+                     const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream);
 /* Tiled INT4 weights (no reference counterpart: the engine's device copy of a weight
  * packed by orchard/quantizer.py:3-78, re-laid once at load). Rows in tiles of 128, k in
  * blocks of 256, each (tile, block) one contiguous 18 KB run of packed nibbles and scales,
@@ -186,18 +193,21 @@ int orch_q4t_linear_swiglu(const void* tiled13, const void* x, void* h, uint32_t
 int orch_q4t_qkv_rope(const void* tiled_qkv, const void* x, uint32_t M, uint32_t K, uint32_t H,
                       uint32_t num_heads, const int32_t* pos, const int32_t* slots,
                       const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
-                      void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
-                      const float* lora_b, uint32_t lora_r, void* stream);
+                      void* k_cache, void* v_cache, uint32_t max_seq, uint32_t num_slots,
+                      const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream);
 /* Decode attention over the device KV cache (orchard/model.py:117-137): for each row m and
  * head h, softmax(q.K[0..pos] / sqrt(hd)) . V[0..pos]. q, out fp16 [M, num_heads*head_dim].
- * Long rows are split over positions; the split partials go to `workspace` (fp32,
- * orch_attention_workspace_bytes() bytes). */
+ * The caches hold num_slots slots; row m reads slot slots[m] (NULL = m). A row whose slot
+ * is outside [0, num_slots) or whose position is outside [0, max_seq) reads nothing, is not
+ * written, and sets device check bit 8 / 2. Long rows are split over positions; the split
+ * partials go to `workspace` (fp32, orch_attention_workspace_bytes() bytes). */
 size_t orch_attention_workspace_bytes(uint32_t M, uint32_t num_heads, uint32_t head_dim,
                                       uint32_t max_seq);
 int orch_attention_decode(const void* q, const void* k_cache, const void* v_cache,
                           const int32_t* pos, const int32_t* slots, void* out, uint32_t M,
                           uint32_t num_heads, uint32_t head_dim, uint32_t max_seq,
-                          void* workspace, size_t workspace_bytes, void* stream);
+                          uint32_t num_slots, void* workspace, size_t workspace_bytes,
+                          void* stream);
 /* INT4 GEMMs with fp16 activations and at least `m` rows run on the tcgen05 tensor-core
  * kernel (TMEM accumulators, TMA-fed activations); fewer rows use the mma.sync decode
  * kernel. 0 disables the tensor-core kernel. Default 17 (ORCHARD_TC_MIN_M overrides). */
@@ -208,10 +218,11 @@ int orch_set_tc_min_m(uint32_t m);
  * num_units records of four int32 (row0, rows, slot, pos0): rows row0 .. row0 + rows - 1
  * (1..64 of them) belong to cache slot `slot` at positions pos0, pos0 + 1, ..., and their
  * K/V are already in the cache; each row attends to positions 0..its own. Rows in no unit are
- * not written. Tensor-core kernel: head_dim 128 only (ORCH_ERR_UNSUPPORTED otherwise). */
+ * not written; a unit whose slot is outside [0, num_slots) is skipped and sets device check
+ * bit 8. Tensor-core kernel: head_dim 128 only (ORCH_ERR_UNSUPPORTED otherwise). */
 int orch_attention_prefill(const void* q, const void* k_cache, const void* v_cache, const int32_t* units,
                            uint32_t num_units, void* out, uint32_t M, uint32_t num_heads, uint32_t head_dim,
-                           uint32_t max_seq, void* stream);
+                           uint32_t max_seq, uint32_t num_slots, void* stream);
 /* Batched-decode INT4 GEMMs on tiled weights (orch_q4t_*, 9..64 activation rows): mode 0
  * (default) always uses the per-tile tensor-core kernel, 1 the persistent stream-K kernel
  * (work split evenly over two CTAs per SM, split tiles summed by a fix-up pass), 2 picks
@@ -245,12 +256,14 @@ int orch_sample_rows(const float* logits, uint32_t M, uint32_t V, float temperat
  * partials exceed the array fails with ORCH_ERR_UNSUPPORTED. Every call on a device uses the
  * same array and leaves its partials there; each call writes every partial it reads, so no
  * clearing is needed, but calls whose execution overlaps on one GPU (for example on two
- * streams) race and must be ordered by the caller. */
+ * streams) race and must be ordered by the caller. Rows rejected by the position or slot
+ * check set their bits in a flag word that also lives inside the library; orch_device_check
+ * reports it. */
 size_t orch_attention_noalloc_max_bytes(void);
 int orch_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                   const int32_t* pos, const int32_t* slots, void* out,
                                   uint32_t M, uint32_t num_heads, uint32_t head_dim,
-                                  uint32_t max_seq, void* stream);
+                                  uint32_t max_seq, uint32_t num_slots, void* stream);
 /* Row argmax of fp32 logits [M, V] (first index of the maximum, as np.argmax;
  * orchard/model.py:244-246). */
 int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, void* stream);

@@ -73,24 +73,25 @@ _SIGS = {
     "orch_q4_linear_resid": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_q4_linear_swiglu": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_q4_qkv_rope": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u32,
-                                _vp, _vp, _vp, _u32, _vp, _vp, _u32, _vp]),
+                                _vp, _vp, _vp, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_q4t_bytes": (_sz, [_u32, _u32]),
     "orch_q4t_pack": (_i32, [_vp, _vp, _u32, _u32, _vp, _vp]),
     "orch_q4t_gemm": (_i32, [_vp, _vp, _vp, _i32, _u32, _u32, _u32, _vp]),
     "orch_q4t_linear_resid": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_q4t_linear_swiglu": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_q4t_qkv_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u32,
-                                 _vp, _vp, _vp, _u32, _vp, _vp, _u32, _vp]),
+                                 _vp, _vp, _vp, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_attention_workspace_bytes": (_sz, [_u32, _u32, _u32, _u32]),
-    "orch_attention_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _sz, _vp]),
+    "orch_attention_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _sz,
+                                     _vp]),
     "orch_set_tc_min_m": (_i32, [_u32]),
-    "orch_attention_prefill": (_i32, [_vp, _vp, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _u32, _vp]),
+    "orch_attention_prefill": (_i32, [_vp, _vp, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _u32, _u32, _vp]),
     "orch_set_stream_k": (_i32, [_i32]),
     "orch_argmax_pairs": (_i32, [_vp, _u32, _u32, _u32, _vp, _vp]),
     "orch_argmax_merge": (_i32, [_vp, _u32, _u32, _u32, _u32, _vp, _vp]),
     "orch_sample_rows": (_i32, [_vp, _u32, _u32, C.c_float, _vp, _vp, _vp]),
     "orch_attention_noalloc_max_bytes": (_sz, []),
-    "orch_attention_decode_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
+    "orch_attention_decode_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]),
     "orch_argmax_rows": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "orch_embed_rows": (_i32, [_vp, _vp, _i32, _vp, _u32, _u32, _u32, _vp]),
 }

@@ -28,8 +28,15 @@ struct AttnArgs {
   __half* out;
   float* ws;  // [M*nh][S][HD + 2]
   int M, nh, max_seq, S;
+  int num_slots;  // slots in the caches; a row whose slot is outside [0, num_slots) is skipped
   uint32_t* check;
 };
+
+// Cache slot of row m, or -1 when it lies outside the caches (uniform per CTA).
+__device__ __forceinline__ int attn_slot(const AttnArgs& a, int m) {
+  const int slot = a.slots ? a.slots[m] : m;
+  return (slot < 0 || slot >= a.num_slots) ? -1 : slot;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
@@ -47,11 +54,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     if (threadIdx.x == 0) atomicOr(a.check, 2u);
     return;
   }
+  const int slot = attn_slot(a, m);
+  if (slot < 0) {
+    if (threadIdx.x == 0) atomicOr(a.check, 8u);
+    return;
+  }
   const int L = p + 1;
   const int per = (L + a.S - 1) / a.S;
   const int p0 = split * per;
   const int p1 = min(L, p0 + per);
-  const int slot = a.slots ? a.slots[m] : m;
   const size_t base = ((size_t)slot * a.nh + h) * a.max_seq * HD;
   const __half* K = a.kc + base;
   const __half* V = a.vc + base;
@@ -184,7 +195,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
   const int mh = blockIdx.x;
   const int m = mh / a.nh, h = mh - m * a.nh;
   const int p = a.pos[m];
-  if (p < 0 || p >= a.max_seq) return;
+  if (p < 0 || p >= a.max_seq || attn_slot(a, m) < 0) return;  // flagged by attn_decode_kernel
   const float* wp = a.ws + (size_t)mh * a.S * (HD + 2);
   float gmax = -INFINITY;
   for (int s = 0; s < a.S; ++s) gmax = fmaxf(gmax, wp[s * (HD + 2)]);
@@ -240,6 +251,14 @@ __global__ void softmax_rows_kernel(const TI* in, TO* out, int cols) {
 }
 
 // ---- row argmax (first index of the maximum, as np.argmax) ---------------------------------
+// Whether candidate (v, i) beats (best, bi) in np.argmax order: a NaN beats any number, the
+// larger value wins, equal values (or two NaNs) go to the lower index.
+__device__ __forceinline__ bool argmax_better(float v, int i, float best, int bi) {
+  const bool vn = v != v, bn = best != best;
+  if (vn || bn) return vn && (!bn || i < bi);
+  return v > best || (v == best && i < bi);
+}
+
 // PAIRS: also write the row's maximum (as float) and base + index (as float, exact below
 // 2^24) to out_pairs[row] for the vocabulary-split merge.
 template <bool PAIRS>
@@ -262,7 +281,7 @@ __global__ void argmax_rows_kernel(const float* logits, int V, int* out, float2*
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
+    if (argmax_better(ov, oi, best, bi)) {
       best = ov;
       bi = oi;
     }
@@ -281,7 +300,7 @@ __global__ void argmax_rows_kernel(const float* logits, int V, int* out, float2*
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi)) {
+      if (argmax_better(ov, oi, best, bi)) {
         best = ov;
         bi = oi;
       }
@@ -309,11 +328,12 @@ extern "C" size_t orch_attention_workspace_bytes(uint32_t M, uint32_t num_heads,
 
 extern "C" int orch_attention_decode(const void* q, const void* k_cache, const void* v_cache,
                                      const int32_t* pos, const int32_t* slots, void* out, uint32_t M,
-                                     uint32_t num_heads, uint32_t head_dim, uint32_t max_seq,
+                                     uint32_t num_heads, uint32_t head_dim, uint32_t max_seq, uint32_t num_slots,
                                      void* workspace, size_t workspace_bytes, void* stream) {
   if (M == 0) return ORCH_OK;
   ORCH_REQUIRE(q && k_cache && v_cache && pos && out, "attention_decode: null pointer");
-  ORCH_REQUIRE(num_heads > 0 && max_seq > 0, "attention_decode: empty shape");
+  ORCH_REQUIRE(num_heads > 0 && max_seq > 0 && num_slots > 0 && num_slots <= 0x7fffffffu,
+               "attention_decode: empty shape");
   ORCH_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
                "attention_decode: head_dim must be 32, 64 or 128");
   AttnArgs a;
@@ -326,8 +346,9 @@ extern "C" int orch_attention_decode(const void* q, const void* k_cache, const v
   a.M = (int)M;
   a.nh = (int)num_heads;
   a.max_seq = (int)max_seq;
+  a.num_slots = (int)num_slots;
   a.S = attn_splits(a.M, a.nh, a.max_seq);
-  a.check = device_check_word();
+  ORCH_CHECK_WORD(a.check);
   const size_t need = orch_attention_workspace_bytes(M, num_heads, head_dim, max_seq);
   ORCH_REQUIRE(workspace_bytes >= need && (need == 0 || workspace != nullptr),
                "attention_decode: workspace too small");
@@ -526,6 +547,12 @@ static int noalloc_setup(int dev, NoAllocState** out) {
   return ORCH_OK;
 }
 
+uint32_t* noalloc_check_word(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  return g_noalloc[dev].check;
+}
+
 static int noalloc_splits(int M, int nh, int max_seq, int sms) {
   const int pairs = M * nh;
   int S = std::max(1, (4 * sms + pairs - 1) / pairs);
@@ -539,10 +566,12 @@ extern "C" size_t orch_attention_noalloc_max_bytes(void) { return orch::kNoAlloc
 
 extern "C" int orch_attention_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                              const int32_t* pos, const int32_t* slots, void* out, uint32_t M,
-                                             uint32_t num_heads, uint32_t head_dim, uint32_t max_seq, void* stream) {
+                                             uint32_t num_heads, uint32_t head_dim, uint32_t max_seq,
+                                             uint32_t num_slots, void* stream) {
   if (M == 0) return ORCH_OK;
   ORCH_REQUIRE(q && k_cache && v_cache && pos && out, "attention_decode_noalloc: null pointer");
-  ORCH_REQUIRE(num_heads > 0 && max_seq > 0, "attention_decode_noalloc: empty shape");
+  ORCH_REQUIRE(num_heads > 0 && max_seq > 0 && num_slots > 0 && num_slots <= 0x7fffffffu,
+               "attention_decode_noalloc: empty shape");
   ORCH_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
                "attention_decode_noalloc: head_dim must be 32, 64 or 128");
   int dev = 0;
@@ -560,6 +589,7 @@ extern "C" int orch_attention_decode_noalloc(const void* q, const void* k_cache,
   a.M = (int)M;
   a.nh = (int)num_heads;
   a.max_seq = (int)max_seq;
+  a.num_slots = (int)num_slots;
   a.S = orch::noalloc_splits(a.M, a.nh, a.max_seq, st->sms);
   a.check = st->check;
   a.ws = st->scratch;

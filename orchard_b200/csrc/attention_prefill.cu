@@ -38,6 +38,7 @@ struct PfArgs {
   const int4* units;  // (row0, rows, slot, pos0)
   __half* out;
   int M, nh, max_seq;
+  int num_slots;  // slots in the caches
   uint32_t* check;
 };
 
@@ -70,8 +71,12 @@ __global__ void __launch_bounds__(128, 3) attn_prefill_kernel(const PfArgs a) {
   const int h = blockIdx.y;
   const int row0 = u.x, n = u.y, slot = u.z, p0 = u.w;
   const int plast = p0 + n - 1;
-  if (n < 1 || n > kPfRows || row0 < 0 || row0 + n > a.M || p0 < 0 || plast >= a.max_seq || slot < 0) {
+  if (n < 1 || n > kPfRows || row0 < 0 || row0 + n > a.M || p0 < 0 || plast >= a.max_seq) {
     if (threadIdx.x == 0) atomicOr(a.check, 2u);
+    return;
+  }
+  if (slot < 0 || slot >= a.num_slots) {
+    if (threadIdx.x == 0) atomicOr(a.check, 8u);
     return;
   }
   const int H = a.nh * kPfHD;
@@ -252,11 +257,12 @@ using namespace orch;
 // orchard/model.py:112-144).
 extern "C" int orch_attention_prefill(const void* q, const void* k_cache, const void* v_cache, const int32_t* units,
                                       uint32_t num_units, void* out, uint32_t M, uint32_t num_heads,
-                                      uint32_t head_dim, uint32_t max_seq, void* stream) {
+                                      uint32_t head_dim, uint32_t max_seq, uint32_t num_slots, void* stream) {
   if (num_units == 0 || M == 0) return ORCH_OK;
   ORCH_REQUIRE(q && k_cache && v_cache && units && out, "attention_prefill: null pointer");
   ORCH_REQUIRE(((uintptr_t)units & 15) == 0, "attention_prefill: units must be 16-byte aligned");
-  ORCH_REQUIRE(num_heads > 0 && num_heads <= 65535 && max_seq > 0, "attention_prefill: bad shape");
+  ORCH_REQUIRE(num_heads > 0 && num_heads <= 65535 && max_seq > 0 && num_slots > 0 && num_slots <= 0x7fffffffu,
+               "attention_prefill: bad shape");
   if (head_dim != (uint32_t)kPfHD) return fail(ORCH_ERR_UNSUPPORTED, "attention_prefill: head_dim must be 128");
   static bool attr_done[64] = {};
   const int dev = device_index();
@@ -273,7 +279,8 @@ extern "C" int orch_attention_prefill(const void* q, const void* k_cache, const 
   a.M = (int)M;
   a.nh = (int)num_heads;
   a.max_seq = (int)max_seq;
-  a.check = device_check_word();
+  a.num_slots = (int)num_slots;
+  ORCH_CHECK_WORD(a.check);
   ORCH_CUDA(launch_k_serial(attn_prefill_kernel, dim3(num_units, num_heads), dim3(128), kPfSmem, as_stream(stream),
                             dim3(0, 0, 0), a));
   return check_launch("attention_prefill");

@@ -133,13 +133,27 @@ extern "C" int orch_device_name(char* buf, size_t len) {
 
 extern "C" int orch_device_check(uint32_t* flags_out, void* stream) {
   ORCH_REQUIRE(flags_out, "device_check: null output");
-  uint32_t* w = device_check_word();
-  if (!w) return fail(ORCH_ERR_NOT_INITIALIZED, "device_check: no device state");
+  *flags_out = 0;
+  const int d = device_index();
+  if (d < 0 || d >= 64) return fail(ORCH_ERR_NOT_INITIALIZED, "device_check: no current device");
   cudaStream_t st = as_stream(stream);
-  ORCH_CUDA(cudaMemcpyAsync(flags_out, w, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
-  ORCH_CUDA(cudaStreamSynchronize(st));
-  ORCH_CUDA(cudaMemsetAsync(w, 0, sizeof(uint32_t), st));
-  ORCH_CUDA(cudaStreamSynchronize(st));
+  // The allocation-free attention entry point flags into its own word inside the library
+  // (it may not allocate the shared one); report both. Reading them allocates nothing once
+  // either exists.
+  uint32_t* words[2] = {g_check[d], noalloc_check_word(d)};
+  if (words[0] == nullptr && words[1] == nullptr) {
+    words[0] = device_check_word();
+    if (!words[0]) return fail(ORCH_ERR_NOT_INITIALIZED, "device_check: no device state");
+  }
+  for (uint32_t* w : words) {
+    if (w == nullptr) continue;
+    uint32_t v = 0;
+    ORCH_CUDA(cudaMemcpyAsync(&v, w, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    ORCH_CUDA(cudaStreamSynchronize(st));
+    ORCH_CUDA(cudaMemsetAsync(w, 0, sizeof(uint32_t), st));
+    ORCH_CUDA(cudaStreamSynchronize(st));
+    *flags_out |= v;
+  }
   return ORCH_OK;
 }
 
@@ -308,7 +322,8 @@ static int linear_swiglu(const void* w13, const void* s13, bool tiled, const voi
 static int qkv_rope(const void* wqkv, const void* sqkv, bool tiled, const void* x, uint32_t M, uint32_t K, uint32_t H,
                     uint32_t num_heads, const int32_t* pos, const int32_t* slots, const float* cos_tab,
                     const float* sin_tab, uint32_t max_pos, void* q_out, void* k_cache, void* v_cache,
-                    uint32_t max_seq, const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream) {
+                    uint32_t max_seq, uint32_t num_slots, const float* lora_t, const float* lora_b, uint32_t lora_r,
+                    void* stream) {
   if (M == 0) return ORCH_OK;
   int rc = check_q4w(wqkv, sqkv, x, K, tiled);
   if (rc) return rc;
@@ -317,7 +332,8 @@ static int qkv_rope(const void* wqkv, const void* sqkv, bool tiled, const void* 
   const uint32_t hd = H / num_heads;
   ORCH_REQUIRE(hd % 2 == 0, "q4_qkv_rope: head_dim must be even");
   ORCH_REQUIRE(H < 65536, "q4_qkv_rope: H must be below 65536");
-  ORCH_REQUIRE(max_seq > 0 && max_pos > 0, "q4_qkv_rope: empty cache");
+  ORCH_REQUIRE(max_seq > 0 && max_pos > 0 && num_slots > 0, "q4_qkv_rope: empty cache");
+  ORCH_REQUIRE(num_slots <= 0x7fffffffu, "q4_qkv_rope: num_slots out of range");
   QArgs a = base_args(wqkv, sqkv, x, ORCH_F16, M, K, 3 * H);
   a.tiled = tiled;
   a.out = q_out;
@@ -326,6 +342,7 @@ static int qkv_rope(const void* wqkv, const void* sqkv, bool tiled, const void* 
   a.hd = (int)hd;
   a.hd_magic = (uint32_t)((0x100000000ull + hd - 1) / hd);
   a.max_seq = (int)max_seq;
+  a.num_slots = (int)num_slots;
   a.max_pos = (int)max_pos;
   a.pos = pos;
   a.slots = slots;
@@ -352,10 +369,10 @@ extern "C" int orch_q4_linear_swiglu(const void* w13, const void* s13, const voi
 extern "C" int orch_q4_qkv_rope(const void* wqkv, const void* sqkv, const void* x, uint32_t M, uint32_t K,
                                 uint32_t H, uint32_t num_heads, const int32_t* pos, const int32_t* slots,
                                 const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
-                                void* k_cache, void* v_cache, uint32_t max_seq, const float* lora_t,
-                                const float* lora_b, uint32_t lora_r, void* stream) {
+                                void* k_cache, void* v_cache, uint32_t max_seq, uint32_t num_slots,
+                                const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream) {
   return qkv_rope(wqkv, sqkv, false, x, M, K, H, num_heads, pos, slots, cos_tab, sin_tab, max_pos, q_out, k_cache,
-                  v_cache, max_seq, lora_t, lora_b, lora_r, stream);
+                  v_cache, max_seq, num_slots, lora_t, lora_b, lora_r, stream);
 }
 
 // ---- tiled-layout forms (weights re-laid by orch_q4t_pack) ----------------------------------
@@ -389,8 +406,8 @@ extern "C" int orch_q4t_linear_swiglu(const void* tiled13, const void* x, void* 
 extern "C" int orch_q4t_qkv_rope(const void* tiled_qkv, const void* x, uint32_t M, uint32_t K, uint32_t H,
                                  uint32_t num_heads, const int32_t* pos, const int32_t* slots, const float* cos_tab,
                                  const float* sin_tab, uint32_t max_pos, void* q_out, void* k_cache, void* v_cache,
-                                 uint32_t max_seq, const float* lora_t, const float* lora_b, uint32_t lora_r,
-                                 void* stream) {
+                                 uint32_t max_seq, uint32_t num_slots, const float* lora_t, const float* lora_b,
+                                 uint32_t lora_r, void* stream) {
   return qkv_rope(tiled_qkv, nullptr, true, x, M, K, H, num_heads, pos, slots, cos_tab, sin_tab, max_pos, q_out,
-                  k_cache, v_cache, max_seq, lora_t, lora_b, lora_r, stream);
+                  k_cache, v_cache, max_seq, num_slots, lora_t, lora_b, lora_r, stream);
 }

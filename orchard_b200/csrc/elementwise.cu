@@ -326,7 +326,8 @@ extern "C" int orch_embedding_ex(const void* ids, const void* weights, int w_dt,
   cudaStream_t st = as_stream(stream);
   const size_t n = (size_t)num_tokens * hidden_dim;
   const int g = grid_for(n, 256);
-  uint32_t* chk = device_check_word();
+  uint32_t* chk = nullptr;
+  ORCH_CHECK_WORD(chk);
   const int* id = (const int*)ids;
   if (w_dt == ORCH_F16 && out_dt == ORCH_F16)
     ORCH_CUDA(launch_k(embedding_kernel<__half, __half>, dim3(g), dim3(256), 0, st, dim3(0, 0, 0), id, (const __half*)weights, (__half*)out, (int)num_tokens, (int)hidden_dim, (int)vocab, chk));

@@ -182,7 +182,7 @@ uint32_t gemv_max_m() { return 8; }
 template <int EPI>
 int gemv_tiled_run(QArgs a, cudaStream_t st) {
   if (a.M < 1 || a.M > 8 || a.x_f32) return ORCH_ERR_UNSUPPORTED;
-  a.check = device_check_word();
+  ORCH_CHECK_WORD(a.check);
   const int nblk = (a.K + kQ4tBlockK - 1) / kQ4tBlockK;
   const int ctas = (a.N + kGvRows - 1) / kGvRows;
   // split K until there are a few CTAs per SM and each CTA's activations stay small

@@ -22,6 +22,9 @@ int check_launch(const char* what);
 int num_sms();
 int device_index();
 uint32_t* device_check_word();  // per-device flag word, set by kernels' own bounds checks
+// The allocation-free attention entry point's own flag word on device `dev` (null until that
+// entry point has run on the device); orch_device_check reports it with the shared word.
+uint32_t* noalloc_check_word(int dev);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 bool pdl_enabled();  // ORCHARD_PDL=0 in the environment turns programmatic launch off
@@ -70,6 +73,14 @@ cudaError_t launch_k_serial(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
 #define ORCH_REQUIRE(cond, msg)                                  \
   do {                                                           \
     if (!(cond)) return ::orch::fail(ORCH_ERR_INVALID, (msg));   \
+  } while (0)
+
+// dst = this device's check word, or return ORCH_ERR_NOT_INITIALIZED (kernels must never
+// be handed a null flag pointer).
+#define ORCH_CHECK_WORD(dst)                                                                    \
+  do {                                                                                          \
+    (dst) = ::orch::device_check_word();                                                        \
+    if ((dst) == nullptr) return ::orch::fail(ORCH_ERR_NOT_INITIALIZED, "no device state for the current device"); \
   } while (0)
 
 #define ORCH_CUDA(call)                                          \

@@ -338,7 +338,7 @@ int qgemm_run(QArgs a, cudaStream_t st) {
     if (rc != ORCH_ERR_UNSUPPORTED) return rc;
   }
   a.nchunk = (a.K + 127) / 128;
-  a.check = device_check_word();
+  ORCH_CHECK_WORD(a.check);
   const int total_M = a.M;
   int m0 = 0;
   while (m0 < total_M) {

@@ -46,6 +46,7 @@ struct QArgs {
   const int* pos;
   const int* slots;   // cache slot of each row; null: row index (slot0 + local row)
   int slot0;          // with null slots, the first row's index (row blocks advance it)
+  int num_slots;      // slots in the caches: a row whose slot is outside [0, num_slots) is skipped
   const float* cos_tab;
   const float* sin_tab;
   __half* kc;
@@ -233,6 +234,10 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
       *reinterpret_cast<__half2*>(static_cast<__half*>(a.out) + (size_t)n * a.H + rr) = hv;
     } else {
       const int slot = a.slots ? a.slots[n] : a.slot0 + n;
+      if (slot < 0 || slot >= a.num_slots) {
+        atomicOr(a.check, 8u);
+        return;
+      }
       __half* cache = region == 1 ? a.kc : a.vc;
       const size_t off = (((size_t)slot * a.nh + head) * a.max_seq + p) * a.hd + d;
       *reinterpret_cast<__half2*>(cache + off) = hv;

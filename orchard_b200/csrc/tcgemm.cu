@@ -535,7 +535,7 @@ int tc_qgemm_run(QArgs a, cudaStream_t st) {
     return ORCH_ERR_UNSUPPORTED;
   if (((uintptr_t)a.x & 15) != 0 || ((uintptr_t)a.w & 15) != 0 || (!tiled && ((uintptr_t)a.s & 15) != 0))
     return ORCH_ERR_UNSUPPORTED;
-  a.check = device_check_word();
+  ORCH_CHECK_WORD(a.check);
   const int ntile = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : a.M <= 128 ? 128 : 256;
   CUtensorMap mx, mw, ms;
   bool ok = encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,

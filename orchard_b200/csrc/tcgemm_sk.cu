@@ -508,7 +508,7 @@ int tc_sk_run(QArgs a, cudaStream_t st) {
   if (tiles > kSkMaxTiles || (long long)tiles * nblk > (1LL << 30)) return ORCH_ERR_UNSUPPORTED;
   SkWorkspace ws;
   if (sk_workspace(st, &ws) != ORCH_OK) return ORCH_ERR_UNSUPPORTED;
-  a.check = device_check_word();
+  ORCH_CHECK_WORD(a.check);
   const int ntile = a.M <= 16 ? 16 : a.M <= 32 ? 32 : 64;
   CUtensorMap mx;
   if (!encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, kSub,

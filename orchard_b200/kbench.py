@@ -112,7 +112,7 @@ def time_attn(M: int, L: int, reps: int, nh: int = 32, hd: int = 128, max_seq: i
     ws = torch.empty(max(wsb // 4, 1), dtype=torch.float32, device=dev)
     def run(i):
         kc, vc = caches[i % n]
-        call("orch_attention_decode", q, kc, vc, pos, None, out, M, nh, hd, max_seq, ws, wsb,
+        call("orch_attention_decode", q, kc, vc, pos, None, out, M, nh, hd, max_seq, M, ws, wsb,
              torch.cuda.current_stream().cuda_stream)
 
     us = _graph_time(run, n, reps)
@@ -136,7 +136,7 @@ def time_attn_prefill(seqs: int, L: int, reps: int, nh: int = 32, hd: int = 128,
     out = torch.empty_like(q)
 
     def run(i):
-        call("orch_attention_prefill", q, kc, vc, units, units.shape[0], out, M, nh, hd, max_seq,
+        call("orch_attention_prefill", q, kc, vc, units, units.shape[0], out, M, nh, hd, max_seq, kc.shape[0],
              torch.cuda.current_stream().cuda_stream)
 
     us = _graph_time(run, 1, reps)

@@ -380,6 +380,7 @@ class DecodeEngine:
         # per row (ORCHARD_PREFILL_ATTN=decode)
         self.prefill_attention = os.environ.get("ORCHARD_PREFILL_ATTN", "tc") != "decode"
         nslots = max_batch + (1 if self.split is not None else 0)
+        self.num_slots = nslots
         self.k_cache = torch.zeros((nl, nslots, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.lora_r = 0
@@ -438,17 +439,17 @@ class DecodeEngine:
             if L.tiled:
                 call("orch_q4t_qkv_rope", ptr(L.tqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos), ptr(b.slots),
                      ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc), self.max_seq,
-                     lt, lb, lr, s)
+                     self.num_slots, lt, lb, lr, s)
             else:
                 call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
                      ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
-                     self.max_seq, lt, lb, lr, s)
+                     self.max_seq, self.num_slots, lt, lb, lr, s)
             if units is not None:
                 call("orch_attention_prefill", ptr(b.q), ptr(kc), ptr(vc), ptr(units), units.shape[0],
-                     ptr(b.attn), M, nh, hd, self.max_seq, s)
+                     ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, s)
             else:
                 call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
-                     ptr(b.attn), M, nh, hd, self.max_seq, ptr(b.attn_ws), b.attn_ws_bytes, s)
+                     ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, ptr(b.attn_ws), b.attn_ws_bytes, s)
             lt, lb, lr = self._lora(L, "o", b.attn, M, s, b)
             if L.tiled:
                 call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)

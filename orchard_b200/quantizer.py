@@ -29,7 +29,8 @@ def quantize_q4_0(weight_fp32, group_size: int = 32):
     if w.ndim != 2:
         raise ValueError(f"expected a 2-D [N, K] weight, got shape {w.shape}")
     n, k = w.shape
-    assert k % group_size == 0, f"Input dimension {k} must be divisible by group size {group_size}"
+    if group_size <= 0 or k % group_size != 0:
+        raise ValueError(f"K = {k} is not a whole number of {group_size}-wide scale groups")
     blocks = w.reshape(n, k // group_size, group_size)
     scale = (np.max(np.abs(blocks), axis=2) / 7.0).astype(np.float16)
     scale[scale == 0] = Q4_ZERO_SCALE

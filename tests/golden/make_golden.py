@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Runs in a container where the reference checkout exists (default
-``/root/reference``, override with ``ORCHARD_REFERENCE``); the fixtures it writes are
-committed so the tests never need the reference at run time.
+Runs where a checkout of the reference exists; its path comes from the
+``ORCHARD_REFERENCE`` environment variable (or the first argument). The fixtures it
+writes are committed so the tests never need the reference at run time.
 
 * ``q4_quantizer.npz``   -- the reference ``quantize_q4_0`` (orchard/quantizer.py:3-78)
   on seeded N(0, 0.02) weights and on hand-made edge blocks (all-zero block, exact
@@ -21,7 +21,7 @@ committed so the tests never need the reference at run time.
 The reference's compute backend is Metal; here ``metal_shim.py`` (a literal
 float32 transcription of the Metal kernels) stands in for ``orchard_core``.
 
-Usage:  python tests/golden/make_golden.py
+Usage:  ORCHARD_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
@@ -35,7 +35,7 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("ORCHARD_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ORCHARD_REFERENCE", "")
 
 CONFIG = {
     "hidden_size": 64,
@@ -53,6 +53,8 @@ LORA_R, LORA_ALPHA = 4, 8
 
 
 def load_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "orchard")):
+        raise SystemExit("make_golden.py: set ORCHARD_REFERENCE (or pass the path) to a reference checkout")
     sys.path.insert(0, HERE)
     import metal_shim
     sys.modules["orchard_core"] = metal_shim

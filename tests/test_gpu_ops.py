@@ -280,6 +280,70 @@ def test_argmax_first_max():
     np.testing.assert_array_equal(out.cpu().numpy(), np.argmax(lg, axis=1))
 
 
+def test_argmax_nan_in_any_lane():
+    """np.argmax returns the first NaN of a row. NaNs placed where different threads, warps
+    and lanes of the block reduction hold them (not only thread 0) must still win, the lowest
+    index among several, in both the plain argmax and the (max, id) pairs of the vocabulary
+    split."""
+    V = 32000
+    lg = rng(24).standard_normal((6, V), dtype=np.float32)
+    lg[0, 5] = np.nan                      # thread 5, warp 0
+    lg[1, 1000 + 37] = np.nan              # thread 13 of warp 1, second sweep
+    lg[2, [31999, 4500, 20001]] = np.nan   # three NaNs in different warps: the first wins
+    lg[3, 64] = np.inf                     # an infinity is a number: it wins only without NaN
+    lg[3, 700] = np.nan
+    lg[4, 3] = 50.0                        # no NaN: the plain maximum
+    lg[5, :] = -np.inf
+    lg[5, 31000] = np.nan
+    out = torch.empty(6, dtype=torch.int32, device="cuda")
+    call("orch_argmax_rows", D(lg), 6, V, ptr(out), S())
+    np.testing.assert_array_equal(out.cpu().numpy(), np.argmax(lg, axis=1))
+    pairs = torch.empty((6, 2), dtype=torch.float32, device="cuda")
+    call("orch_argmax_pairs", D(lg), 6, V, 0, ptr(pairs), S())
+    np.testing.assert_array_equal(pairs.cpu().numpy()[:, 1].astype(np.int64), np.argmax(lg, axis=1))
+
+
+def _device_flags():
+    torch.cuda.synchronize()
+    flags = _lib.C.c_uint32(0)
+    call("orch_device_check", _lib.C.byref(flags), None)
+    return int(flags.value)
+
+
+def test_attention_rejects_rows_outside_the_cache():
+    """A row whose slot is outside [0, num_slots) or whose position is outside the cache is
+    skipped (no cache read, output row left as it was) and reported by orch_device_check
+    (slot: bit 8, position: bit 2); the other rows match the oracle. Every index is checked
+    on the device before it is used, so the bad rows touch no memory."""
+    M, nh, hd, max_seq, nslots = 4, 32, 128, 96, 4
+    g = rng(25)
+    kc = g.standard_normal((nslots, nh, max_seq, hd), dtype=np.float32).astype(np.float16)
+    vc = g.standard_normal((nslots, nh, max_seq, hd), dtype=np.float32).astype(np.float16)
+    q = g.standard_normal((M, nh * hd), dtype=np.float32).astype(np.float16)
+    pos = np.array([50, max_seq, 60, 20], np.int32)      # row 1: position past the cache
+    slots = np.array([3, 0, nslots + 2, 1], np.int32)    # row 2: slot past the cache
+    ws_bytes = _lib.lib().orch_attention_workspace_bytes(M, nh, hd, max_seq)
+    ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device="cuda")
+    _device_flags()
+    out = torch.full((M, nh * hd), 7.0, dtype=torch.float16, device="cuda")
+    call("orch_attention_decode", D(q), D(kc), D(vc), D(pos), D(slots), ptr(out),
+         M, nh, hd, max_seq, nslots, ptr(ws), ws_bytes, S())
+    assert _device_flags() == 2 | 8
+    o = out.float().cpu().numpy()
+    assert np.all(o[1] == 7.0) and np.all(o[2] == 7.0)
+    for m in (0, 3):
+        ref = ops.attention_one(q[m].reshape(nh, hd).astype(np.float32),
+                                kc[slots[m], :, :pos[m] + 1].astype(np.float32),
+                                vc[slots[m], :, :pos[m] + 1].astype(np.float32))
+        assert rel_err(o[m].reshape(nh, hd), ref) <= 1e-2
+    # prefill attention: a unit whose slot is outside the cache is skipped the same way
+    units = np.array([[0, 2, 0, 0], [2, 2, nslots, 0]], np.int32)
+    out2 = torch.full((M, nh * hd), 7.0, dtype=torch.float16, device="cuda")
+    call("orch_attention_prefill", D(q), D(kc), D(vc), D(units), 2, ptr(out2), M, nh, hd, max_seq, nslots, S())
+    assert _device_flags() == 8
+    assert np.all(out2.float().cpu().numpy()[2:] == 7.0)
+
+
 # ---------------------------------------------------------------- attention over the KV cache
 @pytest.mark.parametrize("M,L,hd", [(1, 1, 128), (1, 128, 128), (1, 576, 128), (16, 640, 128),
                                     (64, 513, 128), (3, 1500, 64), (2, 40, 32)])
@@ -295,7 +359,7 @@ def test_attention_decode(M, L, hd):
     ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device="cuda")
     out = torch.empty((M, nh * hd), dtype=torch.float16, device="cuda")
     call("orch_attention_decode", D(q), D(kc), D(vc), D(pos), D(slots), ptr(out),
-         M, nh, hd, max_seq, ptr(ws), ws_bytes, S())
+         M, nh, hd, max_seq, M, ptr(ws), ws_bytes, S())
     o = out.float().cpu().numpy()
     for m in range(M):
         sl, L_m = slots[m], pos[m] + 1
@@ -345,11 +409,11 @@ def test_attention_prefill(lens, starts):
     q = g.standard_normal((M, nh * hd), dtype=np.float32).astype(np.float16)
     units = prefill_units(pos, slots)
     out = torch.empty((M, nh * hd), dtype=torch.float16, device="cuda")
-    call("orch_attention_prefill", D(q), D(kc), D(vc), D(units), len(units), ptr(out), M, nh, hd, max_seq, S())
+    call("orch_attention_prefill", D(q), D(kc), D(vc), D(units), len(units), ptr(out), M, nh, hd, max_seq, kc.shape[0], S())
     ws_bytes = _lib.lib().orch_attention_workspace_bytes(M, nh, hd, max_seq)
     ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device="cuda")
     out_d = torch.empty((M, nh * hd), dtype=torch.float16, device="cuda")
-    call("orch_attention_decode", D(q), D(kc), D(vc), D(pos), D(slots), ptr(out_d), M, nh, hd, max_seq, ptr(ws),
+    call("orch_attention_decode", D(q), D(kc), D(vc), D(pos), D(slots), ptr(out_d), M, nh, hd, max_seq, kc.shape[0], ptr(ws),
          ws_bytes, S())
     o, od = out.float().cpu().numpy(), out_d.float().cpu().numpy()
     assert np.all(np.isfinite(o))

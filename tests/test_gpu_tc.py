@@ -90,7 +90,7 @@ def test_tc_fused_epilogues_match_mma_path(M):
         kc = torch.zeros((M, nh, max_seq, hd), dtype=torch.float16, device="cuda")
         vc = torch.zeros_like(kc)
         call("orch_q4_qkv_rope", torch.from_numpy(pq).cuda(), torch.from_numpy(sq).cuda(), torch.from_numpy(x).cuda(),
-             M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, None, None, 0, S())
+             M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, M, None, None, 0, S())
         h = torch.zeros((M, F), dtype=torch.float16, device="cuda")
         call("orch_q4_linear_swiglu", torch.from_numpy(p13).cuda(), torch.from_numpy(s13).cuda(),
              torch.from_numpy(x).cuda(), h, M, H, F, None, None, 0, S())
@@ -136,7 +136,7 @@ def test_tc_fused_epilogues_with_lora_prefill_rows(r):
         kc = torch.zeros((M, nh, max_seq, hd), dtype=torch.float16, device="cuda")
         vc = torch.zeros_like(kc)
         call("orch_q4_qkv_rope", torch.from_numpy(pq).cuda(), torch.from_numpy(sq).cuda(), torch.from_numpy(x).cuda(),
-             M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, lt3, lb3, r, S())
+             M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, M, lt3, lb3, r, S())
         h = torch.zeros((M, F), dtype=torch.float16, device="cuda")
         call("orch_q4_linear_swiglu", torch.from_numpy(p13).cuda(), torch.from_numpy(s13).cuda(),
              torch.from_numpy(x).cuda(), h, M, H, F, lt2, lb2, r, S())

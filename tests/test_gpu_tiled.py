@@ -163,7 +163,7 @@ def test_tiled_rejects_bad_arguments():
     pos = torch.zeros(2, dtype=torch.int32, device="cuda")
     with pytest.raises(_lib.OrchardError):
         call("orch_q4t_qkv_rope", t, x, 2, 4096, 65536, 512, pos, None, small, small, 16, small, small, small, 4,
-             None, None, 0, S())
+             2, None, None, 0, S())
 
 
 @pytest.mark.parametrize("M", [1, 5, 16, 64, 200])
@@ -195,12 +195,12 @@ def test_tiled_fused_match_reference_layout(M, stream_k):
         h = torch.zeros((M, F), dtype=torch.float16, device="cuda")
         res = torch.ones((M, H), dtype=torch.float32, device="cuda")
         if tiled:
-            call("orch_q4t_qkv_rope", tq, x, M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, lt3, lb3, r, S())
+            call("orch_q4t_qkv_rope", tq, x, M, H, H, nh, pos, None, cd, sd, 2048, q, kc, vc, max_seq, M, lt3, lb3, r, S())
             call("orch_q4t_linear_swiglu", t13, x, h, M, H, F, None, None, 0, S())
             call("orch_q4t_linear_resid", t2, h_in, res, M, F, H, lt1, lb1, r, S())
         else:
             call("orch_q4_qkv_rope", torch.from_numpy(pq).cuda(), torch.from_numpy(sq).cuda(), x, M, H, H, nh, pos,
-                 None, cd, sd, 2048, q, kc, vc, max_seq, lt3, lb3, r, S())
+                 None, cd, sd, 2048, q, kc, vc, max_seq, M, lt3, lb3, r, S())
             call("orch_q4_linear_swiglu", torch.from_numpy(p13).cuda(), torch.from_numpy(s13).cuda(), x, h, M, H, F,
                  None, None, 0, S())
             call("orch_q4_linear_resid", torch.from_numpy(p2).cuda(), torch.from_numpy(s2).cuda(), h_in, res, M, F,
@@ -215,6 +215,43 @@ def test_tiled_fused_match_reference_layout(M, stream_k):
             assert np.all(np.abs(a - b) <= ulp + kernel_tol(M) * np.abs(b).max())
         else:
             assert rel_err(a, b) <= kernel_tol(M)
+
+
+@pytest.mark.parametrize("M", [4, 64, 300])
+def test_qkv_append_rejects_slots_outside_the_cache(M):
+    """A row whose cache slot is outside [0, num_slots) still gets its q but appends no K/V
+    and sets device check bit 8; every other row's K/V land exactly where valid slots put
+    them. M = 4 runs the mma.sync GEMV epilogue, 64 the tensor-core register epilogue, 300
+    the receive-buffer epilogue of the prefill tiles."""
+    H, nh, hd, max_seq = 4096, 32, 128, 8
+    g = np.random.default_rng([23, M])
+    pq, sq, _ = weights(3 * H, H)
+    tq = pack_dev(pq, sq)
+    x = torch.from_numpy(g.standard_normal((M, H), dtype=np.float32).astype(np.float16)).cuda()
+    pos = torch.tensor(g.integers(0, max_seq, M), dtype=torch.int32, device="cuda")
+    c, sn = ops.precompute_freqs_cis(hd, 64)
+    cd, sd = torch.from_numpy(c).cuda(), torch.from_numpy(sn).cuda()
+    good = torch.arange(M, dtype=torch.int32, device="cuda")
+    bad = good.clone()
+    bad[1] = M + 5
+    bad[M - 1] = -1
+    res = []
+    for slots in (good, bad):
+        q = torch.zeros((M, H), dtype=torch.float16, device="cuda")
+        kc = torch.zeros((M, nh, max_seq, hd), dtype=torch.float16, device="cuda")
+        vc = torch.zeros_like(kc)
+        call("orch_q4t_qkv_rope", tq, x, M, H, H, nh, pos, slots, cd, sd, 64, q, kc, vc, max_seq, M, None, None, 0,
+             S())
+        torch.cuda.synchronize()
+        flags = _lib.C.c_uint32(0)
+        call("orch_device_check", _lib.C.byref(flags), None)
+        res.append((flags.value, q.cpu(), kc.cpu(), vc.cpu()))
+    (f0, q0, k0, v0), (f1, q1, k1, v1) = res
+    assert f0 == 0 and f1 == 8
+    assert torch.equal(q0, q1)
+    keep = [m for m in range(M) if m not in (1, M - 1)]
+    assert torch.equal(k1[keep], k0[keep]) and torch.equal(v1[keep], v0[keep])
+    assert not k1[[1, M - 1]].any() and not v1[[1, M - 1]].any()
 
 
 def test_tiled_flag_clear_after_runs():
