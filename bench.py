@@ -169,9 +169,17 @@ QGEMM_ARGS = {"orch_q4_qkv_rope": (3, 4, 5, 3, 2), "orch_q4_linear_swiglu": (4, 
               "orch_q4t_linear_resid": (3, 4, 5, 1, 8), "orch_q4t_gemm": (6, 4, 5, 1, 4)}
 
 
-def kernel_profile(llm, B, pos, reps=3):
+SPLIT_FAMILIES = {"orch_q4t_qkv_rope": "attn_proj_gemm (replicated weights)",
+                  "orch_q4t_linear_resid": "attn_proj_gemm (replicated weights)",
+                  "orch_q4t_linear_swiglu": "ffn_vocab_slice_gemm", "orch_q4t_gemm": "ffn_vocab_slice_gemm",
+                  "nccl": "nccl", "orch_attention_decode": "attention"}
+
+
+def kernel_profile(llm, B, pos, reps=3, split=False):
     """Per-kernel-family device time of one eager decode step (CUDA events around each
-    launch on the launching stream), with each family's algorithmic bytes."""
+    launch on the launching stream), with each family's algorithmic bytes. With `split`
+    (the column split) the families are the replicated attention projections, the FFN /
+    vocabulary slice GEMMs, attention, the NCCL collectives and the rest."""
     import torch
 
     from orchard_b200 import _lib
@@ -192,6 +200,23 @@ def kernel_profile(llm, B, pos, reps=3):
 
     import orchard_b200.model as M
     M.call = timed
+    comm = getattr(eng, "_comm", None)
+    saved = {}
+
+    def timed_collective(fn, *args):
+        st = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        rc = fn(*args)
+        b.record(st)
+        fam.setdefault("nccl", []).append((a, b, args))
+        return rc
+
+    if split and comm is not None:
+        for nm in ("all_gather", "reduce_scatter"):
+            saved[nm] = getattr(comm, nm)
+            setattr(comm, nm, lambda *args, _fn=saved[nm]: timed_collective(_fn, *args))
+
     try:
         for _ in range(reps):
             eng.pos[:B].fill_(pos)
@@ -199,8 +224,17 @@ def kernel_profile(llm, B, pos, reps=3):
         torch.cuda.synchronize()
     finally:
         M.call = orig
+        for nm, fn in saved.items():
+            setattr(comm, nm, fn)
     L = pos + 1
     out = {}
+    if split:
+        for name, ev in fam.items():
+            key = SPLIT_FAMILIES.get(name, "other")
+            d = out.setdefault(key, {"ms": 0.0, "launches": 0})
+            d["ms"] += sum(a.elapsed_time(b) for a, b, _ in ev) / reps
+            d["launches"] += len(ev) // reps
+        return out
     for name, ev in fam.items():
         ms = sum(a.elapsed_time(b) for a, b, _ in ev) / reps
         n = len(ev) // reps
@@ -233,7 +267,7 @@ def time_prefill_lora(llm, reps=3, seqs=8, length=512, rank=16, seed=11):
 
     eng = llm.engine
     H = eng.cfg.hidden_size
-    g = np.random.default_rng([20261201, 5, seed])
+    g = np.random.default_rng([20261201, 5, seed, seqs])
     per_layer = {li: {m: ((g.standard_normal((H, rank)) * 0.01).astype(np.float32),
                           (g.standard_normal((rank, H)) * 0.01).astype(np.float32) * 2.0)
                       for m in ("wq", "wv")} for li in range(eng.cfg.num_hidden_layers)}
@@ -258,103 +292,164 @@ def time_prefill_lora(llm, reps=3, seqs=8, length=512, rank=16, seed=11):
     lora = 2.0 * 32 * 2 * tokens * (H * rank + rank * H)
     flops = lin + attn + lora
     return {"workload": f"batched prefill {seqs}x{length} tokens, LoRA r={rank} on Q and V", "ms": round(t * 1e3, 3),
-            "tok_s": round(tokens / t, 1), "tflops": round(flops / t / 1e12, 2), "flops": flops}
+            "tok_s": round(tokens / t, 1), "tflops": round(flops / t / 1e12, 2), "flops": flops, "s": t}
 
 
-def time_column_split(cfg, dev, global_batch, steps, warmup, rank, world):
+def time_column_split(cfg, dev, global_batch, steps, warmup, rank, world, check_steps=0):
     """The column split (sequences sharded, FFN and vocabulary projections split by columns,
     two NCCL collectives per layer): global_batch sequences, global_batch / world per rank,
-    512-token prompts, greedy decode steps timed on the device (max over ranks)."""
+    512-token prompts, greedy decode steps timed on the device (max over ranks). With fewer
+    sequences than ranks every rank runs the same sequence (attention replicated), counted
+    once. `check_steps` > 0: before timing, that many eager steps of the split engine are
+    compared with the unsplit engine on the same weights and prompts (same input tokens each
+    step): the tokens of this rank's rows (argmax over the whole vocabulary, merged across
+    ranks) and the logits of its vocabulary slice."""
     import torch
     import torch.distributed as dist
 
-    B = global_batch // world
+    replicated = global_batch < world
+    B = 1 if replicated else global_batch // world
     llm = build_model(cfg, dev, B, seed=4321, group=dist.group.WORLD)  # same weights on every rank
     eng = llm.engine
-    g = np.random.default_rng([20261201, 6, rank])
-    llm.prefill(g.integers(0, cfg["vocab_size"], (B, PROMPT)).tolist())
+    g = np.random.default_rng([20261201, 6, 0 if replicated else rank])
+    prompts = g.integers(0, cfg["vocab_size"], (B, PROMPT)).tolist()
+    llm.prefill(prompts)
+    out = {"global_batch": global_batch, "per_rank_batch": B, "steps": steps,
+           "rows": "the same sequence on every rank" if replicated else "sequences sharded over the ranks"}
+    check = None
+    if check_steps:
+        sp = eng.split
+        last = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)
+        eng.tok_in[:B].copy_(last)
+        tin, tout, lgs = [], [], []
+        for s in range(check_steps):
+            eng.pos[:B].fill_(PROMPT + s)
+            tin.append(eng.tok_in[:B].clone())
+            eng.step(B, logits=True, graph=False)
+            tout.append(eng.tok_out[:B].clone())
+            lgs.append(eng.sdec.logits[rank * B:(rank + 1) * B].clone())
+            eng.tok_in[:B].copy_(eng.tok_out[:B])
+        check = (sp.v0, sp.v1, tin, tout, lgs)
     start = PROMPT + 3 - warmup if warmup <= 3 else PROMPT
     eng.pos[:B].fill_(PROMPT)
-    eng.step(B, logits=True)
+    eng.step(B, logits=True)  # capture the graph (with its NCCL calls) before timing
     torch.cuda.synchronize(dev)
     dist.barrier()
     secs = time_decode(llm, B, steps, warmup, start)
     t = torch.tensor([secs], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs = float(t.item())
+    out.update(tok_s=round(global_batch * steps / secs, 2), ms_per_step=round(secs / steps * 1000, 4))
+    if check_steps:
+        fam = kernel_profile(llm, B, start + warmup + steps // 2, split=True)
+        out["families_ms"] = {k: round(v["ms"], 4) for k, v in fam.items()}
     eng.release_graphs()
     del llm, eng
     torch.cuda.empty_cache()
-    secs = float(t.item())
-    return {"global_batch": global_batch, "per_rank_batch": B, "steps": steps,
-            "tok_s": round(global_batch * steps / secs, 2), "ms_per_step": round(secs / steps * 1000, 4),
-            "collectives_per_layer": 2, "note": "FFN and lm_head column-split over NCCL; attention data-parallel"}
+    if check is not None:
+        v0, v1, tin, tout, lgs = check
+        ref = build_model(cfg, dev, B, seed=4321)  # unsplit, same weights
+        ref.prefill(prompts)
+        re = ref.engine
+        match, total, err = 0, 0, 0.0
+        for s in range(check_steps):
+            re.pos[:B].fill_(PROMPT + s)
+            re.tok_in[:B].copy_(tin[s])
+            re.step(B, logits=True, graph=False)
+            match += int((re.tok_out[:B] == tout[s]).sum().item())
+            total += B
+            full = re.logits[:B, v0:v1]
+            err = max(err, float((lgs[s] - full).abs().max().item() / max(full.abs().max().item(), 1e-30)))
+        del ref, re
+        torch.cuda.empty_cache()
+        st = torch.tensor([match, total], dtype=torch.float64, device=dev)
+        dist.all_reduce(st)
+        e = torch.tensor([err], device=dev)
+        dist.all_reduce(e, op=dist.ReduceOp.MAX)
+        out["check"] = {"steps": check_steps, "tokens_match": bool(st[0].item() == st[1].item()),
+                        "tokens_matched": f"{int(st[0].item())}/{int(st[1].item())}",
+                        "logits_max_rel": float(e.item()),
+                        "against": "unsplit engine, same weights, prompts and input tokens"}
+    return out
 
 
-def cpu_baseline_sample(B, target_s=15.0):
-    """The oracle's decode step on the host cores: a 2-layer 7B-shape slice at batch B with
-    577 cached positions, scaled by 16 to 32 layers (+ the lm_head once)."""
-    import oracle
+class OracleStepSample:
+    """The oracle's decode step (the reference's arithmetic restated in NumPy) on the host
+    cores, measured in bounded samples: one sample is one of the 32 layers of a batch-B step
+    at `L0` cached positions (the GPU arm's mean timed position); the final norm + lm_head
+    is timed once. step time = 32 x (mean layer sample) + head. Weights are random codes with
+    unit-ish scales (timing does not depend on values), dequantised once and kept (the
+    fastest host form of the oracle's GEMMs)."""
 
-    cfg = dict(CFG7B, num_hidden_layers=2)
-    H, F, V = 4096, 11008, 32000
-    g = np.random.default_rng(7)
+    def __init__(self, B: int, L0: int, seed: int = 7):
+        import oracle
 
-    def q(n, k):  # timing does not depend on values: random codes, unit-ish scales
-        return (g.integers(0, 256, (n, k // 2), dtype=np.uint8), np.full((n, k // 32), 0.01, np.float16))
+        self.oracle = oracle
+        H, F, V = 4096, 11008, 32000
+        g = np.random.default_rng(seed)
 
-    layers = [oracle.model.OracleLayer(wq=q(H, H), wk=q(H, H), wv=q(H, H), wo=q(H, H), w1=q(F, H), w3=q(F, H),
-                                       w2=q(H, F), attn_norm=np.ones(H, np.float32), ffn_norm=np.ones(H, np.float32))
-              for _ in range(2)]
-    om = oracle.model.OracleModel(cfg, layers, g.standard_normal((V, H), dtype=np.float32), np.ones(H, np.float32),
-                                  q(V, H))
-    L0 = 576
-    for li in range(2):
+        def q(n, k):
+            return (g.integers(0, 256, (n, k // 2), dtype=np.uint8), np.full((n, k // 32), 0.01, np.float16))
+
+        layer = oracle.model.OracleLayer(wq=q(H, H), wk=q(H, H), wv=q(H, H), wo=q(H, H), w1=q(F, H), w3=q(F, H),
+                                         w2=q(H, F), attn_norm=np.ones(H, np.float32),
+                                         ffn_norm=np.ones(H, np.float32))
+        cfg = dict(CFG7B, num_hidden_layers=1)
+        self.om = oracle.model.OracleModel(cfg, [layer], g.standard_normal((V, H), dtype=np.float32),
+                                           np.ones(H, np.float32), q(V, H), cache_dequant=True)
+        self.B, self.L0 = B, L0
         for b in range(B):
-            om.k_cache[li][b] = g.standard_normal((32, L0, 128), dtype=np.float32)
-            om.v_cache[li][b] = g.standard_normal((32, L0, 128), dtype=np.float32)
-    toks = list(range(B))
-    t_layers, t_head, n = 0.0, 0.0, 0
-    t_start = time.perf_counter()
-    while n < 1 or time.perf_counter() - t_start < target_s:
-        x = om.embed[np.asarray(toks)]
-        cos, sin = om.freqs_cos[[L0] * B], om.freqs_sin[[L0] * B]
+            self.om.k_cache[0][b] = g.standard_normal((32, L0, 128), dtype=np.float32)
+            self.om.v_cache[0][b] = g.standard_normal((32, L0, 128), dtype=np.float32)
+        self.x = self.om.embed[np.arange(B) % V]
+        self.cos, self.sin = self.om.freqs_cos[[L0] * B], self.om.freqs_sin[[L0] * B]
+
+    def layer(self) -> float:
         t0 = time.perf_counter()
-        for li in range(2):
-            x = om.layer_forward(li, x, cos, sin, list(range(B)))
-        t1 = time.perf_counter()
-        om._lin(om.lm_head, oracle.ops.rmsnorm(x, om.norm, 1e-5))
-        t2 = time.perf_counter()
-        for li in range(2):  # keep the cache length fixed
-            for b in range(B):
-                om.k_cache[li][b] = om.k_cache[li][b][:, :L0]
-                om.v_cache[li][b] = om.v_cache[li][b][:, :L0]
-        t_layers += t1 - t0
-        t_head += t2 - t1
-        n += 1
-    step_s = (t_layers / n) * 16 + t_head / n
-    try:
-        import threadpoolctl
-        threads = max((i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()), default=1)
-    except Exception:
-        threads = os.cpu_count() or 1
-    return {"value": B / step_s, "unit": "tok/s", "cores": int(threads),
-            "kind": "port",
-            "sample": f"oracle decode step, batch {B}, 2 of 32 layers at 577 cached positions "
-                      f"(x16 extrapolated) + lm_head, {n} reps, {time.perf_counter() - t_start:.1f}s host time",
+        self.om.layer_forward(0, self.x, self.cos, self.sin, list(range(self.B)))
+        t = time.perf_counter() - t0
+        for b in range(self.B):  # keep the cache at L0 positions
+            self.om.k_cache[0][b] = self.om.k_cache[0][b][:, :self.L0]
+            self.om.v_cache[0][b] = self.om.v_cache[0][b][:, :self.L0]
+        return t
+
+    def head(self) -> float:
+        t0 = time.perf_counter()
+        self.om._lin(self.om.lm_head, self.oracle.ops.rmsnorm(self.x, self.om.norm, 1e-5))
+        return time.perf_counter() - t0
+
+    @staticmethod
+    def cores() -> dict:
+        try:
+            import threadpoolctl
+            blas = max((i.get("num_threads", 1) for i in threadpoolctl.threadpool_info()), default=1)
+        except Exception:
+            blas = None
+        return {"blas_threads": blas, "os_cpu_count": os.cpu_count()}
+
+
+def timed_positions(steps: int, warmup: int):
+    """First warm-up position, first and last timed positions of the GPU arm."""
+    start = PROMPT + 3 - warmup if warmup <= 3 else PROMPT
+    return start, start + warmup, start + warmup + steps - 1
+
+
+def cpu_baseline_sample(B, L0, target_s=12.0):
+    """cpu_baseline of our arm's line: layer samples for about `target_s` seconds."""
+    smp = OracleStepSample(B, L0)
+    smp.layer()  # warm (dequantises the weights once)
+    head = min(smp.head(), smp.head())
+    ts = []
+    t_start = time.perf_counter()
+    while not ts or time.perf_counter() - t_start < target_s:
+        ts.append(smp.layer())
+    step_s = 32 * float(np.mean(ts)) + head
+    cores = OracleStepSample.cores()
+    return {"value": B / step_s, "unit": "tok/s", "cores": int(cores["blas_threads"] or cores["os_cpu_count"] or 1),
+            "kind": "port", **cores,
+            "sample": f"oracle decode step, batch {B}, {L0} cached positions: {len(ts)} samples of one of the 32 "
+                      f"layers ({np.mean(ts) * 1e3:.0f} ms each) x 32 + final norm and lm_head ({head * 1e3:.0f} ms)",
             "step_s": step_s}
-
-
-# DRAM bytes (read + write) per decode step of each kernel family at batch 64, from one ncu
-# capture of a 2-layer model of these shapes scaled to the layer count (the capture, its
-# command and the per-launch figures are summarised in profiles/decode_b64_traffic.md).
-_TRAFFIC_B64 = {"qgemm": {"per_layer": 28.88e6 + 2 * 19.45e6 + 51.29e6, "once": 74.46e6}}
-
-
-def _traffic(family, layers, batch):
-    t = _TRAFFIC_B64.get(family)
-    if t is None or batch != 64:
-        return None
-    return round(t["per_layer"] * layers + t["once"])
 
 
 def run_ours(args):
@@ -379,9 +474,9 @@ def run_ours(args):
     llm.prefill(prompts)
     torch.cuda.synchronize(dev)
     prefill_s = time.perf_counter() - t0
-    start = PROMPT + 3 - args.warmup if args.warmup <= 3 else PROMPT
-    assert start + args.warmup + args.steps <= MAX_SEQ, "steps + warmup exceed the 640-position decode window"
-    # capture graphs before timing
+    start, first, last = timed_positions(args.steps, args.warmup)
+    assert last < MAX_SEQ, "steps + warmup exceed the 640-position decode window"
+    # capture the graph before timing
     eng.pos[:B].fill_(PROMPT)
     eng.step(B, logits=True)
     torch.cuda.synchronize(dev)
@@ -400,7 +495,7 @@ def run_ours(args):
     value = tokens / secs_max
 
     # kernel families of one step at the mean timed position; roofline of the dominant one
-    mid = start + args.warmup + args.steps // 2
+    mid = first + args.steps // 2
     prof = kernel_profile(llm, B, mid)
     dom = max(("qgemm", "attention"), key=lambda k: prof.get(k, {"ms": 0})["ms"])
     peaks = {}
@@ -413,18 +508,20 @@ def run_ours(args):
     achieved = d["bytes"] / (d["ms"] / 1000.0) / 1e9
     step_ms = secs_max / args.steps * 1000.0
     prof_ms = sum(v["ms"] for v in prof.values())
+    fam = {k: {"ms": round(v["ms"], 4), "GBps": round(v["bytes"] / (v["ms"] / 1000.0) / 1e9, 1) if v["bytes"] else None,
+               "launches": v["launches"]} for k, v in prof.items()}
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": "measured" if peaks else "fallback",
-                "traffic": _traffic(dom, args.layers, B), "launches_per_step": d["launches"],
-                "bytes_per_step": d["bytes"], "share_of_eager_step": round(d["ms"] / prof_ms, 3),
-                "families_ms": {k: round(v["ms"], 4) for k, v in prof.items()}}
+                "traffic": None, "traffic_note": "DRAM bytes of the same kernels from ncu are summarised in profiles/",
+                "launches_per_step": d["launches"], "bytes_per_step": d["bytes"],
+                "share_of_eager_step": round(d["ms"] / prof_ms, 3), "families": fam}
     step_bytes = sum(v["bytes"] for v in prof.values())
     line = {"metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights x fp16 activations, fp32 accumulate",
             "data": "synthetic (seeded random-init weights N(0,0.02) packed by the reference rule; random prompts)",
             "config": {"workload": f"llama-2-7b-shape INT4 batched decode, batch {B}/GPU, prompt {PROMPT}, "
-                                   f"positions {start + args.warmup}..{start + args.warmup + args.steps - 1}",
+                                   f"positions {first}..{last}",
                        "model": "llama-2-7b-shape (32 layers, hidden 4096, 32x128 heads, FFN 11008, vocab 32000)",
                        "global_batch": B * world, "seq_len": MAX_SEQ, "parallelism": f"dp{world} (sequence replicas)",
                        "l2": "no flush needed: each step streams 3.7 GB of weights + KV (> 126 MB L2)"},
@@ -433,13 +530,6 @@ def run_ours(args):
             "gpu_launches": eng.kernel_launches_per_step(B) * args.steps}
     if rank == 0:
         line["clocks"] = clk.summary()
-    # the column split, measured beside the replicas (N > 1)
-    if world > 1 and not args.no_column_split:
-        del llm, eng
-        torch.cuda.empty_cache()
-        line["column_split"] = time_column_split(cfg, dev, B, min(args.steps, 32), args.warmup, rank, world)
-        llm = build_model(cfg, dev, max_b, seed=1234 + rank)
-        eng = llm.engine
     # per-batch lines (N = 1 only)
     if world == 1:
         per = {}
@@ -451,7 +541,28 @@ def run_ours(args):
             sb = time_decode(llm, b, args.steps, args.warmup, start)
             per[str(b)] = {"tok_s": round(b * args.steps / sb, 2), "ms_per_step": round(sb / args.steps * 1000, 4)}
         line["per_batch"] = per
-    # end to end through the public API: generate_batch_ids with per-step H2D/D2H
+    # the column split, measured beside the replicas (N > 1): global batch 64 (with the token
+    # check against the unsplit engine and the per-family breakdown), 16 and 1
+    if world > 1 and not args.no_column_split:
+        del llm, eng
+        torch.cuda.empty_cache()
+        splits = {}
+        for gb in (B, 16, 1):
+            if gb != B and (gb in splits or (gb >= world and gb % world)):
+                continue
+            splits[str(gb)] = time_column_split(cfg, dev, gb, min(args.steps, 32), args.warmup, rank, world,
+                                                check_steps=8 if gb == B else 0)
+        line["column_split"] = {"note": "FFN and lm_head column-split over NCCL; attention data-parallel "
+                                        "(replicated attention weights); two collectives per layer",
+                                "by_global_batch": splits}
+        llm = build_model(cfg, dev, max_b, seed=1234 + rank)
+        eng = llm.engine
+        llm.prefill(prompts)
+    # end to end through the public API: generate_batch_ids with per-step H2D/D2H; the
+    # batch's decode graph is captured before (as at N = 1, where the timing above did it)
+    eng.pos[:B].fill_(PROMPT)
+    eng.step(B, logits=True)
+    torch.cuda.synchronize(dev)
     stats = {}
     e2e_prompts = g.integers(0, cfg["vocab_size"], (B, PROMPT)).tolist()
     llm.generate_batch_ids(e2e_prompts, max_tokens=args.steps, temperature=0, ignore_eos=True, stats=stats)
@@ -460,16 +571,33 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     line["e2e"] = {"value": round(B * stats["steps"] * world / float(tt.item()), 2), "unit": "tok/s",
                    "h2d_bytes_per_step": stats["h2d_bytes_per_step"], "d2h_bytes_per_step": stats["d2h_bytes_per_step"],
-                   "api": "Llama.generate_batch_ids (greedy), decode phase",
+                   "api": "Llama.generate_batch_ids (greedy), decode phase; graph captured before timing",
                    "prefill_s": round(stats["prefill_s"], 2)}
-    pf = time_prefill_lora(llm)
+    # config 5: 8 sequences x 512 tokens with Q/V LoRA, sequences sharded over the ranks
+    seqs = max(1, 8 // world)
+    pf = time_prefill_lora(llm, seqs=seqs)
+    pt = torch.tensor([pf["s"]], device=dev)
+    if world > 1:
+        dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+    t_pf = float(pt.item())
     peaks_bf16 = float(peaks.get("bf16_tflops", 1590.0))
-    pf["frac_of_bf16_peak"] = round(pf["tflops"] / peaks_bf16, 4)
-    line["prefill_config5"] = pf
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_baseline_sample(B)
-        cb.pop("step_s", None)
-        line["cpu_baseline"] = cb
+    flops = pf["flops"] * world
+    line["prefill_config5"] = {"workload": f"batched prefill {seqs * world}x512 tokens, LoRA r=16 on Q and V, "
+                                           f"{seqs} sequence(s) per GPU",
+                               "ms": round(t_pf * 1e3, 3), "tok_s": round(seqs * world * 512 / t_pf, 1),
+                               "tflops": round(flops / t_pf / 1e12, 2), "flops": flops,
+                               "frac_of_bf16_peak": round(flops / t_pf / 1e12 / (peaks_bf16 * world), 4),
+                               "time": "max over ranks, median of 3"}
+    if rank == 0 and world == 1:
+        from orchard_b200 import kbench
+        line["gemv_sweep"] = {"peak_GBps": peak, "cases": kbench.gemv_sweep(reps=30, peak_gbs=peak),
+                              "what": "orch_q4t_gemm (INT4 g32, tiled) and orch_gemm_q8_pc (INT8 per channel), "
+                                      "fp16 out, graph-timed over weight copies > 4 x L2"}
+        line["elementwise_config2"] = kbench.elementwise_config(reps=50)
+        if not args.no_cpu_baseline:
+            cb = cpu_baseline_sample(B, (first + last) // 2)
+            cb.pop("step_s", None)
+            line["cpu_baseline"] = cb
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -478,19 +606,40 @@ def run_ours(args):
 
 
 def run_reference(args):
+    """The reference arm: the oracle's decode step on the host cores (the reference's compute
+    backend is Apple Metal; its CPU path is the NumPy arithmetic restated in oracle/), same
+    workload, metric and positions as our arm. Each step is a bounded sample: one of the 32
+    layers of the batch's decode step; the value extrapolates 32 layers + the lm_head."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    cb = cpu_baseline_sample(args.batch, target_s=max(5.0, min(60.0, 0.2 * (args.steps + args.warmup))))
-    line = {"metric": METRIC, "value": round(cb["value"], 4), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(cb["step_s"] * 1000, 2), "higher_is_better": True,
+    start, first, last = timed_positions(args.steps, args.warmup)
+    L0 = (first + last) // 2
+    smp = OracleStepSample(args.batch, L0)
+    head = min(smp.head(), smp.head())
+    for _ in range(max(1, args.warmup)):
+        smp.layer()
+    ts = [smp.layer() for _ in range(args.steps)]
+    layer_s = float(np.mean(ts))
+    step_s = 32 * layer_s + head
+    value = args.batch / step_s
+    cores = OracleStepSample.cores()
+    sample = (f"oracle decode step, batch {args.batch}, {L0} cached positions: {args.steps} timed samples of one of "
+              f"the 32 layers ({layer_s * 1e3:.0f} ms each) x 32 + final norm and lm_head ({head * 1e3:.0f} ms)")
+    line = {"metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(layer_s * 1000, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 NumPy arithmetic",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"llama-2-7b-shape INT4 batched decode, batch {args.batch}, prompt {PROMPT}",
+            "config": {"workload": f"llama-2-7b-shape INT4 batched decode, batch {args.batch}, prompt {PROMPT}, "
+                                   f"positions {first}..{last} (sampled at {L0})",
                        "model": "llama-2-7b-shape", "global_batch": args.batch, "seq_len": MAX_SEQ,
                        "parallelism": "host cores"},
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": round(cb["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "step_unit": "one of the 32 layers of a decode step (bounded sample); value = batch / (32 x layer + head)",
+            "extrapolated_ms_per_step": round(step_s * 1000, 1),
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "kind": "port",
+                             "cores": int(cores["blas_threads"] or cores["os_cpu_count"] or 1), **cores,
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's compute backend is Apple Metal (unavailable on this box); its CPU path "
                     "(orchard/model.py with the kernel arithmetic in NumPy) is the oracle port"}
     print(json.dumps(line), flush=True)

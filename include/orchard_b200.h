@@ -120,6 +120,10 @@ int orch_gemm_q8_0_ex(const void* w, const void* scales, const void* in, int in_
 int orch_binary_ex(int op, const void* a, const void* b, void* c, int dt, uint32_t size,
                    void* stream);
 int orch_silu_ex(const void* in, void* out, int dt, uint32_t size, void* stream);
+/* SwiGLU in one pass, out = silu(gate) * up (orchard/model.py:179-180, which runs run_silu
+ * then run_mul, elementwise.metal:13-30): fp32 arithmetic, one rounding to dt on store. */
+int orch_swiglu_ex(const void* gate, const void* up, void* out, int dt, uint32_t size,
+                   void* stream);
 int orch_softmax_ex(const void* in, int in_dt, void* out, int out_dt, uint32_t rows,
                     uint32_t cols, void* stream);
 int orch_embedding_ex(const void* ids, const void* weights, int w_dt, void* out, int out_dt,

@@ -63,6 +63,7 @@ _SIGS = {
     "orch_gemm_q8_0_ex": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _u32, _u32, _u32, _vp]),
     "orch_binary_ex": (_i32, [_i32, _vp, _vp, _vp, _i32, _u32, _vp]),
     "orch_silu_ex": (_i32, [_vp, _vp, _i32, _u32, _vp]),
+    "orch_swiglu_ex": (_i32, [_vp, _vp, _vp, _i32, _u32, _vp]),
     "orch_softmax_ex": (_i32, [_vp, _i32, _vp, _i32, _u32, _u32, _vp]),
     "orch_embedding_ex": (_i32, [_vp, _vp, _i32, _vp, _i32, _u32, _u32, _u32, _vp]),
     "orch_quantize_q4_0": (_i32, [_vp, _i32, _vp, _vp, _u32, _u32, _vp]),

@@ -427,51 +427,59 @@ class DecodeEngine:
         prefill_units for these rows) routes attention to the tensor-core prefill kernel,
         which reads each sequence's keys once per 64 rows instead of once per row."""
         b = bufs if bufs is not None else self.dec
-        cfg, s = self.cfg, _stream()
-        H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
-        nh, hd, eps = cfg.num_attention_heads, cfg.head_dim, cfg.rms_norm_eps
+        cfg = self.cfg
         call("orch_embed_rows", ptr(b.tok_in), ptr(self.embed), F16 if self.embed.dtype == torch.float16 else F32,
-             ptr(b.x), M, H, V, s)
-        for li, L in enumerate(self.layers):
-            kc, vc = self.k_cache[li], self.v_cache[li]
-            call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.attn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
-            lt, lb, lr = self._lora(L, "qkv", b.xn, M, s, b)
-            if L.tiled:
-                call("orch_q4t_qkv_rope", ptr(L.tqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos), ptr(b.slots),
-                     ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc), self.max_seq,
-                     self.num_slots, lt, lb, lr, s)
-            else:
-                call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
-                     ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
-                     self.max_seq, self.num_slots, lt, lb, lr, s)
-            if units is not None:
-                call("orch_attention_prefill", ptr(b.q), ptr(kc), ptr(vc), ptr(units), units.shape[0],
-                     ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, s)
-            else:
-                call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
-                     ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, ptr(b.attn_ws), b.attn_ws_bytes, s)
-            lt, lb, lr = self._lora(L, "o", b.attn, M, s, b)
-            if L.tiled:
-                call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
-            else:
-                call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
-            call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.ffn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
-            if self.split is not None:
-                if "gu" in L.lora or "down" in L.lora:
-                    raise ValueError("LoRA on the FFN projections is not supported with the column split")
-                sb = self.sdec if b is self.dec else self._split_bufs(b)
-                ffn_column_split(self._split_ops, self._comm, L, sb, M)
-                continue
-            lt, lb, lr = self._lora(L, "gu", b.xn, M, s, b)
-            if L.tiled:
-                call("orch_q4t_linear_swiglu", ptr(L.t13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
-            else:
-                call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
-            lt, lb, lr = self._lora(L, "down", b.h, M, s, b)
-            if L.tiled:
-                call("orch_q4t_linear_resid", ptr(L.t2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
-            else:
-                call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
+             ptr(b.x), M, cfg.hidden_size, cfg.vocab_size, _stream())
+        for li in range(len(self.layers)):
+            self.run_layer(li, M, b, units)
+
+    def run_layer(self, li: int, M: int, bufs: Optional[RowBuffers] = None, units: Optional[torch.Tensor] = None):
+        """Layer `li` (LlamaLayer.forward, orchard/model.py:78-195) on the fp32 residual rows
+        [0, M) of `bufs`.x in place, at the rows' positions and cache slots."""
+        b = bufs if bufs is not None else self.dec
+        cfg, s = self.cfg, _stream()
+        H, F = cfg.hidden_size, cfg.intermediate_size
+        nh, hd, eps = cfg.num_attention_heads, cfg.head_dim, cfg.rms_norm_eps
+        L = self.layers[li]
+        kc, vc = self.k_cache[li], self.v_cache[li]
+        call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.attn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
+        lt, lb, lr = self._lora(L, "qkv", b.xn, M, s, b)
+        if L.tiled:
+            call("orch_q4t_qkv_rope", ptr(L.tqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos), ptr(b.slots),
+                 ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc), self.max_seq,
+                 self.num_slots, lt, lb, lr, s)
+        else:
+            call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
+                 ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
+                 self.max_seq, self.num_slots, lt, lb, lr, s)
+        if units is not None:
+            call("orch_attention_prefill", ptr(b.q), ptr(kc), ptr(vc), ptr(units), units.shape[0],
+                 ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, s)
+        else:
+            call("orch_attention_decode", ptr(b.q), ptr(kc), ptr(vc), ptr(b.pos), ptr(b.slots),
+                 ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, ptr(b.attn_ws), b.attn_ws_bytes, s)
+        lt, lb, lr = self._lora(L, "o", b.attn, M, s, b)
+        if L.tiled:
+            call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
+        else:
+            call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
+        call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.ffn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
+        if self.split is not None:
+            if "gu" in L.lora or "down" in L.lora:
+                raise ValueError("LoRA on the FFN projections is not supported with the column split")
+            sb = self.sdec if b is self.dec else self._split_bufs(b)
+            ffn_column_split(self._split_ops, self._comm, L, sb, M)
+            return
+        lt, lb, lr = self._lora(L, "gu", b.xn, M, s, b)
+        if L.tiled:
+            call("orch_q4t_linear_swiglu", ptr(L.t13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
+        else:
+            call("orch_q4_linear_swiglu", ptr(L.w13), ptr(L.s13), ptr(b.xn), ptr(b.h), M, H, F, lt, lb, lr, s)
+        lt, lb, lr = self._lora(L, "down", b.h, M, s, b)
+        if L.tiled:
+            call("orch_q4t_linear_resid", ptr(L.t2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
+        else:
+            call("orch_q4_linear_resid", ptr(L.w2), ptr(L.s2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
 
     def run_head(self, M: int, temperature: float = 0.0):
         """Final RMSNorm, INT4 lm_head (fp32 logits) and the next token into tok_out: the

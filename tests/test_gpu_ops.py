@@ -223,6 +223,15 @@ def test_swiglu_elementwise(B):
         np.testing.assert_allclose(t.float().cpu().numpy(), ref, atol=tol * 4, rtol=tol * 4)
         call("orch_binary_ex", 0, ptr(gd), ptr(ud), ptr(t), dt, n, S())
         np.testing.assert_allclose(t.float().cpu().numpy(), ops.add(g.astype(npdt), u.astype(npdt)), atol=tol * 8, rtol=tol)
+        # the one-pass form: fp32 silu(g) * u, rounded once
+        f = torch.empty_like(gd)
+        call("orch_swiglu_ex", ptr(gd), ptr(ud), ptr(f), dt, n, S())
+        ref1 = ops.mul(ops.silu(g.astype(npdt).astype(np.float32)), u.astype(npdt).astype(np.float32))
+        np.testing.assert_allclose(f.float().cpu().numpy(), ref1, atol=tol * 4, rtol=tol * 4)
+        if dt == F16:  # odd length and offset views take the scalar kernel
+            call("orch_swiglu_ex", ptr(gd) + 2, ptr(ud) + 2, ptr(f), dt, n - 3, S())
+            np.testing.assert_allclose(f.float().cpu().numpy().reshape(-1)[: n - 3], ref1.reshape(-1)[1:n - 2],
+                                       atol=tol * 4, rtol=tol * 4)
 
 
 def test_full_test_kats():
