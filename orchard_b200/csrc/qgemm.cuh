@@ -199,7 +199,9 @@ __device__ __forceinline__ void epi_apply(const QArgs& a, int n, int idx, float 
       v0 += lora(n, 0, idx, F);
       v1 += lora(n, 1, idx, F);
     }
-    const float si = v0 / (1.0f + expf(-v0));
+    // silu(g) = g / (1 + e^-g); the fast divide is within 2 ulp (the IEEE divide is a
+    // subroutine that dominated the decode epilogue); exp(-g) = inf gives 0, silu's limit
+    const float si = __fdividef(v0, 1.0f + expf(-v0));
     static_cast<__half*>(a.out)[(size_t)n * F + idx] = __float2half_rn(si * v1);
   } else {  // EPI_QKV
     const int half_hd = a.hd >> 1;

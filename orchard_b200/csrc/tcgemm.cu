@@ -400,15 +400,18 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     // Prefill tiles (128-256 rows) keep the receive-buffer path below, where all eleven warps
     // share the epilogue (with four warps the LoRA terms of 256 rows took 8x512-token prefill
     // from 162 to 264 ms).
-    if (warp < 4 && !bad) {
+    // Warps w and w + 4 share TMEM lane quarter w % 4 and take alternate groups of 16
+    // activation rows (one warp per quarter ran this latency-bound code ~2x slower).
+    if (warp < kWarpsDq && !bad) {
+      const int quarter = warp & 3;
 #pragma unroll 1
-      for (int cc = 0; cc < Mp; cc += 16) {
+      for (int cc = (warp >> 2) * 16; cc < Mp; cc += 32) {
         uint32_t r[16];
-        tmem_ld16(tmem_d + ((uint32_t)(32 * warp) << 16) + (uint32_t)cc, r);
+        tmem_ld16(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cc, r);
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-        tc_epilogue16<EPI>(a, R0, warp, lane, v, cc);
+        tc_epilogue16<EPI>(a, R0, quarter, lane, v, cc);
       }
     }
     tc_fence_before();
@@ -422,12 +425,13 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   cg::cluster_group cl = cg::this_cluster();
   cl.sync();
   float* recv = reinterpret_cast<float*>(sm);
-  if (warp < 4) {  // TMEM lanes 32w..32w+31 belong to warp w (w = 0..3)
+  if (warp < kWarpsDq) {  // TMEM lanes 32 (w % 4) .. + 31; warps w, w + 4 alternate row groups
+    const int quarter = warp & 3;
 #pragma unroll 1
-    for (int cc = 0; cc < Mp; cc += 16) {
+    for (int cc = (warp >> 2) * 16; cc < Mp; cc += 32) {
       uint32_t r[16];
-      tmem_ld16(tmem_d + ((uint32_t)(32 * warp) << 16) + (uint32_t)cc, r);
-      float* dst = epi_dest<EPI, kTcRows>(cl, recv, Mp, KS, ks, tid, cc);
+      tmem_ld16(tmem_d + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cc, r);
+      float* dst = epi_dest<EPI, kTcRows>(cl, recv, Mp, KS, ks, quarter * 32 + lane, cc);
       const int pitch = epi_pitch<EPI, kTcRows>(KS);
 #pragma unroll
       for (int j = 0; j < 16; ++j)
