@@ -163,7 +163,8 @@ def time_decode(llm, B, steps, warmup, start_pos):
 
 
 # INT4 GEMM entry points: argument index of M, K and N, N multiplier, output bytes per element
-QGEMM_ARGS = {"orch_q4_qkv_rope": (3, 4, 5, 3, 2), "orch_q4_linear_swiglu": (4, 5, 6, 2, 1),
+QGEMM_ARGS = {"orch_q4t_rms_qkv_rope": (5, 6, 7, 3, 2), "orch_q4t_rms_linear_swiglu": (6, 7, 8, 2, 1),
+              "orch_q4_qkv_rope": (3, 4, 5, 3, 2), "orch_q4_linear_swiglu": (4, 5, 6, 2, 1),
               "orch_q4_linear_resid": (4, 5, 6, 1, 8), "orch_gemm_q4_0_ex": (8, 6, 7, 1, 4),
               "orch_q4t_qkv_rope": (2, 3, 4, 3, 2), "orch_q4t_linear_swiglu": (3, 4, 5, 2, 1),
               "orch_q4t_linear_resid": (3, 4, 5, 1, 8), "orch_q4t_gemm": (6, 4, 5, 1, 4)}

@@ -199,6 +199,23 @@ int orch_q4t_qkv_rope(const void* tiled_qkv, const void* x, uint32_t M, uint32_t
                       const float* cos_tab, const float* sin_tab, uint32_t max_pos, void* q_out,
                       void* k_cache, void* v_cache, uint32_t max_seq, uint32_t num_slots,
                       const float* lora_t, const float* lora_b, uint32_t lora_r, void* stream);
+/* RMSNorm fused in front of the tiled Q/K/V (+ RoPE + KV append) and gate/up (+ SwiGLU)
+ * projections: the reference's rms_norm -> projection pair (orchard/model.py:86-101,160-172;
+ * orchard/kernels/rmsnorm.metal:23-35). x is the fp32 residual [M, K], norm_w fp32 [K] (both
+ * 16-byte aligned); the activations are fp16(x * rsqrt(sum(x^2) / K + eps) * norm_w). Up to 8
+ * rows, the GEMV computes the norm itself (one launch; xn is not written); with more rows the
+ * normalised rows go to the fp16 scratch xn [M, K] and the tensor-core GEMM reads them. No
+ * LoRA term (its x.A needs xn first: use orch_rmsnorm_ex and the unfused entry points). */
+int orch_q4t_rms_qkv_rope(const void* tiled_qkv, const float* x, const float* norm_w, float eps,
+                          void* xn, uint32_t M, uint32_t K, uint32_t H, uint32_t num_heads,
+                          const int32_t* pos, const int32_t* slots, const float* cos_tab,
+                          const float* sin_tab, uint32_t max_pos, void* q_out, void* k_cache,
+                          void* v_cache, uint32_t max_seq, uint32_t num_slots, void* stream);
+int orch_q4t_rms_linear_swiglu(const void* tiled13, const float* x, const float* norm_w, float eps,
+                               void* xn, void* h, uint32_t M, uint32_t K, uint32_t F, void* stream);
+/* Rows up to which the orch_q4t_* entry points take the GEMV (8; ORCHARD_GEMV_MAX_M in the
+ * environment may lower it); above it they run on the tcgen05 tensor-core GEMM. */
+uint32_t orch_gemv_max_rows(void);
 /* Decode attention over the device KV cache (orchard/model.py:117-137): for each row m and
  * head h, softmax(q.K[0..pos] / sqrt(hd)) . V[0..pos]. q, out fp16 [M, num_heads*head_dim].
  * The caches hold num_slots slots; row m reads slot slots[m] (NULL = m). A row whose slot

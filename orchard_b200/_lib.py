@@ -82,6 +82,10 @@ _SIGS = {
     "orch_q4t_linear_swiglu": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _vp]),
     "orch_q4t_qkv_rope": (_i32, [_vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u32,
                                  _vp, _vp, _vp, _u32, _u32, _vp, _vp, _u32, _vp]),
+    "orch_q4t_rms_qkv_rope": (_i32, [_vp, _vp, _vp, _f32, _vp, _u32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _u32,
+                                     _vp, _vp, _vp, _u32, _u32, _vp]),
+    "orch_q4t_rms_linear_swiglu": (_i32, [_vp, _vp, _vp, _f32, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "orch_gemv_max_rows": (_u32, []),
     "orch_attention_workspace_bytes": (_sz, [_u32, _u32, _u32, _u32]),
     "orch_attention_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _sz,
                                      _vp]),

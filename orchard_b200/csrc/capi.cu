@@ -411,3 +411,81 @@ extern "C" int orch_q4t_qkv_rope(const void* tiled_qkv, const void* x, uint32_t 
   return qkv_rope(tiled_qkv, nullptr, true, x, M, K, H, num_heads, pos, slots, cos_tab, sin_tab, max_pos, q_out,
                   k_cache, v_cache, max_seq, num_slots, lora_t, lora_b, lora_r, stream);
 }
+
+// ---- RMSNorm fused in front of the tiled Q/K/V and gate/up projections ----------------------
+// M <= 8 rows: the GEMV normalises the fp32 residual itself (no separate launch, xn untouched);
+// more rows: RMSNorm into xn, then the tensor-core GEMM (two launches, as before).
+static int rms_args(QArgs& a, const float* x, const float* norm_w, float eps) {
+  ORCH_REQUIRE(x && norm_w, "rmsnorm-fused GEMM: null pointer");
+  ORCH_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)norm_w & 15) == 0,
+               "rmsnorm-fused GEMM: x and norm_w must be 16-byte aligned");
+  a.x = x;
+  a.x_f32 = 1;
+  a.norm_w = norm_w;
+  a.norm_eps = eps;
+  return ORCH_OK;
+}
+
+extern "C" int orch_q4t_rms_qkv_rope(const void* tiled_qkv, const float* x, const float* norm_w, float eps, void* xn,
+                                     uint32_t M, uint32_t K, uint32_t H, uint32_t num_heads, const int32_t* pos,
+                                     const int32_t* slots, const float* cos_tab, const float* sin_tab,
+                                     uint32_t max_pos, void* q_out, void* k_cache, void* v_cache, uint32_t max_seq,
+                                     uint32_t num_slots, void* stream) {
+  if (M == 0) return ORCH_OK;
+  ORCH_REQUIRE(xn, "rms_qkv_rope: null xn");
+  if (M <= gemv_tiled_limit()) {
+    // the argument checks of the unfused form, on the fp16 scratch as a stand-in for x
+    int rc = check_q4w(tiled_qkv, nullptr, xn, K, true);
+    if (rc) return rc;
+    ORCH_REQUIRE(pos && cos_tab && sin_tab && q_out && k_cache && v_cache, "rms_qkv_rope: null pointer");
+    ORCH_REQUIRE(num_heads > 0 && H % num_heads == 0 && (H / num_heads) % 2 == 0 && H < 65536,
+                 "rms_qkv_rope: bad head shape");
+    ORCH_REQUIRE(max_seq > 0 && max_pos > 0 && num_slots > 0 && num_slots <= 0x7fffffffu, "rms_qkv_rope: empty cache");
+    QArgs a = base_args(tiled_qkv, nullptr, x, ORCH_F32, M, K, 3 * H);
+    a.tiled = 1;
+    if ((rc = rms_args(a, x, norm_w, eps))) return rc;
+    const uint32_t hd = H / num_heads;
+    a.out = q_out;
+    a.H = (int)H;
+    a.nh = (int)num_heads;
+    a.hd = (int)hd;
+    a.hd_magic = (uint32_t)((0x100000000ull + hd - 1) / hd);
+    a.max_seq = (int)max_seq;
+    a.num_slots = (int)num_slots;
+    a.max_pos = (int)max_pos;
+    a.pos = pos;
+    a.slots = slots;
+    a.cos_tab = cos_tab;
+    a.sin_tab = sin_tab;
+    a.kc = static_cast<__half*>(k_cache);
+    a.vc = static_cast<__half*>(v_cache);
+    rc = gemv_tiled_run<EPI_QKV>(a, as_stream(stream));
+    if (rc != ORCH_ERR_UNSUPPORTED) return rc;
+  }
+  int rc = orch_rmsnorm_ex(x, ORCH_F32, norm_w, ORCH_F32, xn, ORCH_F16, eps, K, M, stream);
+  if (rc) return rc;
+  return orch_q4t_qkv_rope(tiled_qkv, xn, M, K, H, num_heads, pos, slots, cos_tab, sin_tab, max_pos, q_out, k_cache,
+                           v_cache, max_seq, num_slots, nullptr, nullptr, 0, stream);
+}
+
+extern "C" int orch_q4t_rms_linear_swiglu(const void* tiled13, const float* x, const float* norm_w, float eps,
+                                          void* xn, void* h, uint32_t M, uint32_t K, uint32_t F, void* stream) {
+  if (M == 0 || F == 0) return ORCH_OK;
+  ORCH_REQUIRE(xn && h, "rms_linear_swiglu: null pointer");
+  if (F % 16 != 0) return fail(ORCH_ERR_UNSUPPORTED, "rms_linear_swiglu: F must be a multiple of 16");
+  if (M <= gemv_tiled_limit()) {
+    int rc = check_q4w(tiled13, nullptr, xn, K, true);
+    if (rc) return rc;
+    QArgs a = base_args(tiled13, nullptr, x, ORCH_F32, M, K, 2 * F);
+    a.tiled = 1;
+    if ((rc = rms_args(a, x, norm_w, eps))) return rc;
+    a.out = h;
+    rc = gemv_tiled_run<EPI_SWIGLU>(a, as_stream(stream));
+    if (rc != ORCH_ERR_UNSUPPORTED) return rc;
+  }
+  int rc = orch_rmsnorm_ex(x, ORCH_F32, norm_w, ORCH_F32, xn, ORCH_F16, eps, K, M, stream);
+  if (rc) return rc;
+  return orch_q4t_linear_swiglu(tiled13, xn, h, M, K, F, nullptr, nullptr, 0, stream);
+}
+
+extern "C" uint32_t orch_gemv_max_rows(void) { return gemv_tiled_limit(); }

@@ -100,12 +100,52 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tiled_kernel(const QArgs a) {
 
   // activations x[n][k] for n < M, k in this CTA's K range (zero past K), natural order
   const int kbeg = b0 * kQ4tBlockK, units = nb * 32;  // 8 halves per unit
-  for (int i = threadIdx.x; i < a.M * units; i += kGvThreads) {
-    const int n = i / units, u = i - n * units;
-    const int k = kbeg + u * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (k < a.K) v = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + (size_t)n * a.K + k));
-    *reinterpret_cast<uint4*>(xs + n * xp + u * 16) = v;
+  if (a.norm_w == nullptr) {
+    for (int i = threadIdx.x; i < a.M * units; i += kGvThreads) {
+      const int n = i / units, u = i - n * units;
+      const int k = kbeg + u * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (k < a.K) v = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + (size_t)n * a.K + k));
+      *reinterpret_cast<uint4*>(xs + n * xp + u * 16) = v;
+    }
+  } else {
+    // The RMSNorm of orchard/kernels/rmsnorm.metal:23-35 fused in front of the projection:
+    // every CTA reads its rows of the fp32 residual whole (L2-resident, 16 KB a row at the 7B
+    // shape) for rsqrt(sum(x^2) / K + eps), then stages fp16(x * rsqrt * gamma) for its K
+    // slice -- the arithmetic of rmsnorm_vec_kernel, summed in another order.
+    __shared__ float red[32];
+    __shared__ float inv_s[8];
+    const float* xr = static_cast<const float*>(a.x);
+    for (int n = 0; n < a.M; ++n) {
+      float ss = 0.f;
+      for (int k = threadIdx.x * 4; k < a.K; k += kGvThreads * 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xr + (size_t)n * a.K + k));
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+      }
+      ss = block_sum(ss, red);
+      if (threadIdx.x == 0) inv_s[n] = rsqrtf(ss / (float)a.K + a.norm_eps);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.M * units; i += kGvThreads) {
+      const int n = i / units, u = i - n * units;
+      const int k = kbeg + u * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (k < a.K) {
+        const float inv = inv_s[n];
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(xr + (size_t)n * a.K + k));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(xr + (size_t)n * a.K + k + 4));
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.norm_w + k));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.norm_w + k + 4));
+        v.x = h2_bits(__floats2half2_rn(x0.x * inv * g0.x, x0.y * inv * g0.y));
+        v.y = h2_bits(__floats2half2_rn(x0.z * inv * g0.z, x0.w * inv * g0.w));
+        v.z = h2_bits(__floats2half2_rn(x1.x * inv * g1.x, x1.y * inv * g1.y));
+        v.w = h2_bits(__floats2half2_rn(x1.z * inv * g1.z, x1.w * inv * g1.w));
+      }
+      *reinterpret_cast<uint4*>(xs + n * xp + u * 16) = v;
+    }
   }
   __syncthreads();
 
@@ -181,7 +221,7 @@ uint32_t gemv_max_m() { return 8; }
 
 template <int EPI>
 int gemv_tiled_run(QArgs a, cudaStream_t st) {
-  if (a.M < 1 || a.M > 8 || a.x_f32) return ORCH_ERR_UNSUPPORTED;
+  if (a.M < 1 || a.M > 8 || (a.x_f32 && a.norm_w == nullptr)) return ORCH_ERR_UNSUPPORTED;
   ORCH_CHECK_WORD(a.check);
   const int nblk = (a.K + kQ4tBlockK - 1) / kQ4tBlockK;
   const int ctas = (a.N + kGvRows - 1) / kGvRows;

@@ -294,16 +294,6 @@ int dispatch_nt(const QArgs& a, int KS, size_t smem, cudaStream_t st) {
 
 int rows_per_cta(int M) { return (M > 32) ? 128 : 64; }
 
-// Rows up to which tiled INT4 GEMMs take the mma.sync GEMV (gemv.cu); ORCHARD_GEMV_MAX_M
-// overrides (0: always the tensor-core kernel).
-uint32_t gemv_tiled_limit() {
-  static const uint32_t v = [] {
-    const char* e = std::getenv("ORCHARD_GEMV_MAX_M");
-    return e ? (uint32_t)std::max(0, std::atoi(e)) : gemv_max_m();
-  }();
-  return std::min(v, gemv_max_m());
-}
-
 // CTAs per SM the cluster K-split aims for (more resident warps keep more weight bytes in
 // flight); ORCHARD_QGEMM_CTAS_PER_SM overrides.
 int ks_target() {
@@ -315,6 +305,16 @@ int ks_target() {
 }
 
 }  // namespace
+
+// Rows up to which tiled INT4 GEMMs take the mma.sync GEMV (gemv.cu); ORCHARD_GEMV_MAX_M
+// overrides (0: always the tensor-core kernel).
+uint32_t gemv_tiled_limit() {
+  static const uint32_t v = [] {
+    const char* e = std::getenv("ORCHARD_GEMV_MAX_M");
+    return e ? (uint32_t)std::max(0, std::atoi(e)) : gemv_max_m();
+  }();
+  return std::min(v, gemv_max_m());
+}
 
 // Splits M into blocks of <= 64 rows that fit shared memory, picks the cluster K-split,
 // and launches. `advance` moves the per-row pointers of an args block by `m` rows.

@@ -56,6 +56,10 @@ struct QArgs {
   int lora_r;
   uint32_t* check;
   int tiled;          // w is in the tiled INT4 layout (s unused); tensor-core path only
+  // RMSNorm prologue (GEMV for M <= 8 only): x is the fp32 residual [M, K]; the kernel uses
+  // fp16(x * rsqrt(sum(x^2) / K + norm_eps) * norm_w) as its activations
+  const float* norm_w;
+  float norm_eps;
 };
 
 template <int WF, int EPI>
@@ -77,6 +81,8 @@ uint32_t tc_min_m();
 template <int EPI>
 int gemv_tiled_run(QArgs a, cudaStream_t st);
 uint32_t gemv_max_m();
+// Rows up to which tiled INT4 GEMMs take that GEMV (ORCHARD_GEMV_MAX_M may lower it).
+uint32_t gemv_tiled_limit();
 
 namespace cg = cooperative_groups;
 

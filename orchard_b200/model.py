@@ -442,16 +442,22 @@ class DecodeEngine:
         nh, hd, eps = cfg.num_attention_heads, cfg.head_dim, cfg.rms_norm_eps
         L = self.layers[li]
         kc, vc = self.k_cache[li], self.v_cache[li]
-        call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.attn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
-        lt, lb, lr = self._lora(L, "qkv", b.xn, M, s, b)
-        if L.tiled:
-            call("orch_q4t_qkv_rope", ptr(L.tqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos), ptr(b.slots),
-                 ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc), self.max_seq,
-                 self.num_slots, lt, lb, lr, s)
+        if L.tiled and "qkv" not in L.lora:
+            # RMSNorm fused in front of the projection (one launch for up to 8 rows)
+            call("orch_q4t_rms_qkv_rope", ptr(L.tqkv), ptr(b.x), ptr(L.attn_norm), eps, ptr(b.xn), M, H, H, nh,
+                 ptr(b.pos), ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
+                 self.max_seq, self.num_slots, s)
         else:
-            call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
-                 ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
-                 self.max_seq, self.num_slots, lt, lb, lr, s)
+            call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.attn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
+            lt, lb, lr = self._lora(L, "qkv", b.xn, M, s, b)
+            if L.tiled:
+                call("orch_q4t_qkv_rope", ptr(L.tqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos), ptr(b.slots),
+                     ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc), self.max_seq,
+                     self.num_slots, lt, lb, lr, s)
+            else:
+                call("orch_q4_qkv_rope", ptr(L.wqkv), ptr(L.sqkv), ptr(b.xn), M, H, H, nh, ptr(b.pos),
+                     ptr(b.slots), ptr(self.cos), ptr(self.sin), self.max_pos, ptr(b.q), ptr(kc), ptr(vc),
+                     self.max_seq, self.num_slots, lt, lb, lr, s)
         if units is not None:
             call("orch_attention_prefill", ptr(b.q), ptr(kc), ptr(vc), ptr(units), units.shape[0],
                  ptr(b.attn), M, nh, hd, self.max_seq, self.num_slots, s)
@@ -463,6 +469,12 @@ class DecodeEngine:
             call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
         else:
             call("orch_q4_linear_resid", ptr(L.wo), ptr(L.so), ptr(b.attn), ptr(b.x), M, H, H, lt, lb, lr, s)
+        if L.tiled and self.split is None and "gu" not in L.lora:
+            call("orch_q4t_rms_linear_swiglu", ptr(L.t13), ptr(b.x), ptr(L.ffn_norm), eps, ptr(b.xn), ptr(b.h), M,
+                 H, F, s)
+            lt, lb, lr = self._lora(L, "down", b.h, M, s, b)
+            call("orch_q4t_linear_resid", ptr(L.t2), ptr(b.h), ptr(b.x), M, F, H, lt, lb, lr, s)
+            return
         call("orch_rmsnorm_ex", ptr(b.x), F32, ptr(L.ffn_norm), F32, ptr(b.xn), F16, eps, H, M, s)
         if self.split is not None:
             if "gu" in L.lora or "down" in L.lora:
@@ -546,7 +558,11 @@ class DecodeEngine:
 
     def kernel_launches_per_step(self, M: int, logits: bool = True) -> int:
         """Kernels of this library one step launches (for reporting)."""
-        per_layer = 7 + sum(1 for L in self.layers[:1] for _ in L.lora)
+        L0 = self.layers[0]
+        small = M <= _lib.lib().orch_gemv_max_rows()  # the GEMV normalises its own rows
+        per_layer = 7 + len(L0.lora)
+        per_layer -= int(L0.tiled and "qkv" not in L0.lora and small)
+        per_layer -= int(L0.tiled and self.split is None and "gu" not in L0.lora and small)
         if self.split is not None:
             per_layer += 1  # the residual add after the reduce-scatter
         n = 1 + per_layer * len(self.layers)

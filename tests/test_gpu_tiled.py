@@ -254,6 +254,55 @@ def test_qkv_append_rejects_slots_outside_the_cache(M):
     assert not k1[[1, M - 1]].any() and not v1[[1, M - 1]].any()
 
 
+@pytest.mark.parametrize("M", [1, 3, 8, 16])
+def test_rmsnorm_fused_projections_match_unfused(M):
+    """orch_q4t_rms_qkv_rope / orch_q4t_rms_linear_swiglu (RMSNorm computed inside the GEMV for
+    up to 8 rows) against orch_rmsnorm_ex followed by the unfused entry points. The fused norm
+    sums x^2 in another order, so an element of the normalised row may round to the other
+    neighbouring fp16: outputs within 2e-3 of max|ref|; the q / K / V rows and h otherwise
+    identical in layout and position. M = 16 takes the two-launch path (bit-identical)."""
+    H, F, nh, hd, max_seq = 4096, 11008, 32, 128, 16
+    g = np.random.default_rng([29, M])
+    pq, sq, _ = weights(3 * H, H)
+    p13, s13, _ = weights(2 * F, H)
+    tq, t13 = pack_dev(pq, sq), pack_dev(p13, s13)
+    x = torch.from_numpy(g.standard_normal((M, H), dtype=np.float32) * 2.0).cuda()
+    gam = torch.from_numpy((1 + 0.1 * g.standard_normal(H)).astype(np.float32)).cuda()
+    pos = torch.tensor(g.integers(0, max_seq, M), dtype=torch.int32, device="cuda")
+    c, sn = ops.precompute_freqs_cis(hd, 64)
+    cd, sd = torch.from_numpy(c).cuda(), torch.from_numpy(sn).cuda()
+    outs = []
+    for fused in (True, False):
+        xn = torch.zeros((M, H), dtype=torch.float16, device="cuda")
+        q = torch.zeros((M, H), dtype=torch.float16, device="cuda")
+        kc = torch.zeros((M, nh, max_seq, hd), dtype=torch.float16, device="cuda")
+        vc = torch.zeros_like(kc)
+        h = torch.zeros((M, F), dtype=torch.float16, device="cuda")
+        if fused:
+            call("orch_q4t_rms_qkv_rope", tq, x, gam, 1e-5, xn, M, H, H, nh, pos, None, cd, sd, 64, q, kc, vc,
+                 max_seq, M, S())
+            call("orch_q4t_rms_linear_swiglu", t13, x, gam, 1e-5, xn, h, M, H, F, S())
+        else:
+            call("orch_rmsnorm_ex", x, F32, gam, F32, xn, F16, 1e-5, H, M, S())
+            call("orch_q4t_qkv_rope", tq, xn, M, H, H, nh, pos, None, cd, sd, 64, q, kc, vc, max_seq, M, None, None,
+                 0, S())
+            call("orch_q4t_linear_swiglu", t13, xn, h, M, H, F, None, None, 0, S())
+        torch.cuda.synchronize()
+        outs.append([t.float().cpu().numpy() for t in (q, kc, vc, h)])
+    for a, b in zip(*outs):
+        if M > 8:
+            np.testing.assert_array_equal(a, b)
+        else:
+            assert rel_err(a, b) <= 2e-3
+    # the oracle: RMSNorm (orchard/kernels/rmsnorm.metal:23-35), the gate/up projection (rows
+    # interleaved in blocks of 16: 32b + i gate, 32b + 16 + i up) and SwiGLU, within 1e-2
+    xn_ref = ops.rmsnorm(x.cpu().numpy(), gam.cpu().numpy(), 1e-5).astype(np.float16).astype(np.float32)
+    y = ops.gemm_q4_0(p13, s13, xn_ref)
+    j = np.arange(F)
+    gate, up = y[:, 32 * (j // 16) + j % 16], y[:, 32 * (j // 16) + 16 + j % 16]
+    assert rel_err(outs[0][3], ops.mul(ops.silu(gate), up)) <= 1e-2
+
+
 def test_tiled_flag_clear_after_runs():
     flags = _lib.C.c_uint32(0)
     call("orch_device_check", _lib.C.byref(flags), None)
