@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-column-split", action="store_true", help="at N > 1 skip the column-split measurement")
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--only-decode", action="store_true",
+                    help="time the decode step alone (no per-batch, split, e2e, prefill, sweep or CPU sections): "
+                         "for launch-list captures")
     return ap.parse_args()
 
 
@@ -549,6 +552,13 @@ def run_ours(args):
             "gpu_launches": eng.kernel_launches_per_step(B) * args.steps}
     if rank == 0:
         line["clocks"] = clk.summary()
+    if args.only_decode:
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     # per-batch lines (N = 1 only)
     if world == 1:
         per = {}

@@ -196,20 +196,36 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
   const int m = mh / a.nh, h = mh - m * a.nh;
   const int p = a.pos[m];
   if (p < 0 || p >= a.max_seq || attn_slot(a, m) < 0) return;  // flagged by attn_decode_kernel
+  // One thread per output dimension (blockDim.x == HD). The splits are taken HD at a time: each
+  // thread turns one split's running max into its weight f_s = exp(m_s - max) in shared memory,
+  // then every thread sums that group's partials with the loads issued together. (A loop that
+  // read m_s, then l_s, then the partial, split by split, waited one L2 round trip per split:
+  // 11 us per layer at batch 1 with 19 splits.)
+  __shared__ float fsh[HD];
+  __shared__ float red[32];
+  const int d = threadIdx.x;
   const float* wp = a.ws + (size_t)mh * a.S * (HD + 2);
-  float gmax = -INFINITY;
-  for (int s = 0; s < a.S; ++s) gmax = fmaxf(gmax, wp[s * (HD + 2)]);
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < a.S; ++s) {
-      const float ms = wp[s * (HD + 2)];
-      if (ms == -INFINITY) continue;
-      const float f = __expf(ms - gmax);
-      den += f * wp[s * (HD + 2) + 1];
-      num += f * wp[s * (HD + 2) + 2 + d];
+  float lmax = -INFINITY;
+  for (int s = d; s < a.S; s += HD) lmax = fmaxf(lmax, wp[s * (HD + 2)]);
+  const float gmax = block_max(lmax, red);
+  float lden = 0.f, num = 0.f;
+  for (int s0 = 0; s0 < a.S; s0 += HD) {
+    float f = 0.f;
+    if (s0 + d < a.S) {
+      const float ms = wp[(s0 + d) * (HD + 2)];
+      f = ms == -INFINITY ? 0.f : __expf(ms - gmax);
+      lden = fmaf(f, wp[(s0 + d) * (HD + 2) + 1], lden);
     }
-    a.out[(size_t)m * a.nh * HD + h * HD + d] = __float2half_rn(num / den);
+    fsh[d] = f;
+    __syncthreads();
+    const int n = min(HD, a.S - s0);
+    const float* part = wp + (size_t)s0 * (HD + 2) + 2 + d;
+#pragma unroll 8
+    for (int j = 0; j < n; ++j) num = fmaf(fsh[j], part[j * (HD + 2)], num);
+    __syncthreads();
   }
+  const float den = block_sum(lden, red);
+  a.out[(size_t)m * a.nh * HD + h * HD + d] = __float2half_rn(num / den);
 }
 
 static int attn_splits(int M, int nh, int max_seq) {

@@ -109,24 +109,59 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tiled_kernel(const QArgs a) {
       *reinterpret_cast<uint4*>(xs + n * xp + u * 16) = v;
     }
   } else {
-    // The RMSNorm of orchard/kernels/rmsnorm.metal:23-35 fused in front of the projection:
-    // every CTA reads its rows of the fp32 residual whole (L2-resident, 16 KB a row at the 7B
-    // shape) for rsqrt(sum(x^2) / K + eps), then stages fp16(x * rsqrt * gamma) for its K
-    // slice -- the arithmetic of rmsnorm_vec_kernel, summed in another order.
-    __shared__ float red[32];
+    // The RMSNorm of orchard/kernels/rmsnorm.metal:23-35 fused in front of the projection,
+    // rsqrt(sum(x^2) / K + eps) per row of the fp32 residual, then fp16(x * rsqrt * gamma)
+    // staged for this CTA's K slice -- the arithmetic of rmsnorm_vec_kernel, summed in another
+    // order. The KS CTAs splitting K form one cluster: each sums the squares of its own slice
+    // only (all rows in one pass, so M loads are in flight; per row a warp butterfly, then
+    // the four warps as (w0 + w2) + (w1 + w3)), publishes the M partials in shared memory,
+    // and after one cluster barrier every CTA adds the KS partials in rank order, so all of
+    // them scale by the same factor. (Each CTA reading whole rows cost KS times the L2 reads:
+    // 68 us instead of 21 us for the 8-row gate/up launch with its 8-way split.)
+    static_assert(kGvWarps == 4, "the cross-warp sum below is written for four warps");
+    __shared__ float red8[kGvWarps][8];
+    __shared__ float ss_part[8];
     __shared__ float inv_s[8];
     const float* xr = static_cast<const float*>(a.x);
-    for (int n = 0; n < a.M; ++n) {
-      float ss = 0.f;
-      for (int k = threadIdx.x * 4; k < a.K; k += kGvThreads * 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(xr + (size_t)n * a.K + k));
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
+    const int kend = min(a.K, kbeg + nb * kQ4tBlockK);
+    float ss[8];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) ss[n] = 0.f;
+    for (int k = kbeg + threadIdx.x * 4; k < kend; k += kGvThreads * 4) {
+      float4 v[8];
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+        if (n < a.M) v[n] = __ldg(reinterpret_cast<const float4*>(xr + (size_t)n * a.K + k));
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+        if (n < a.M) {
+          ss[n] = fmaf(v[n].x, v[n].x, ss[n]);
+          ss[n] = fmaf(v[n].y, v[n].y, ss[n]);
+          ss[n] = fmaf(v[n].z, v[n].z, ss[n]);
+          ss[n] = fmaf(v[n].w, v[n].w, ss[n]);
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      if (n < a.M) {
+        const float t = warp_sum(ss[n]);
+        if ((threadIdx.x & 31) == 0) red8[threadIdx.x >> 5][n] = t;
       }
-      ss = block_sum(ss, red);
-      if (threadIdx.x == 0) inv_s[n] = rsqrtf(ss / (float)a.K + a.norm_eps);
+    }
+    __syncthreads();
+    if (threadIdx.x < a.M) {
+      const int n = threadIdx.x;
+      ss_part[n] = (red8[0][n] + red8[2][n]) + (red8[1][n] + red8[3][n]);
+    }
+    // Every CTA of the cluster reaches this barrier and the one before the split-K exchange
+    // below, so a peer's ss_part is read before that peer can exit.
+    cg::cluster_group clu = cg::this_cluster();
+    clu.sync();
+    if (threadIdx.x < a.M) {
+      const int n = threadIdx.x;
+      float t = 0.f;
+      for (int r = 0; r < KS; ++r) t += *clu.map_shared_rank(&ss_part[n], (unsigned)r);
+      inv_s[n] = rsqrtf(t / (float)a.K + a.norm_eps);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < a.M * units; i += kGvThreads) {
