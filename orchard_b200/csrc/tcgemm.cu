@@ -8,13 +8,15 @@
 // D[128 weight rows, NTILE tokens] (fp32, TMEM) += A[128, 16] . B[NTILE, 16]^T per MMA, in
 // stages of 128 k, with four warp roles per CTA:
 //  * a weight producer (one thread) streams packed 128-row x 128-k tiles and their scales
-//    (one 8 KB bulk copy per stage from the tiled layout, or 2-D TMA boxes from the
-//    reference layout) into a 6-stage ring, starting before griddepcontrol.wait;
+//    (per stage an 8 KB and a 1 KB bulk copy from the tiled layout, or 2-D TMA boxes from
+//    the reference layout) into a 6-stage ring, starting before griddepcontrol.wait;
 //  * an activation producer (one thread) streams the [NTILE, 128] fp16 activation tiles
 //    (two TMA boxes of 64 k, SWIZZLE_128B; rows past M and k past K read as zero);
 //  * eight dequantisation warps turn each packed tile into fp16 (q - 8) * scale with the
 //    magic-exponent trick and store it with tcgen05.st into a ring of A tiles in tensor
-//    memory (3-4 stages deep), one weight row per TMEM lane;
+//    memory (3-4 stages deep), one weight row per TMEM lane. They form two groups of four
+//    (one warp per TMEM lane quarter) that take alternate stages, so two stages' chains of
+//    wait, dequantise, store and arrive run at once;
 //  * one thread issues eight tcgen05.mma.kind::f16 per stage with A from tensor memory and
 //    B (activations) from shared memory; tcgen05.commit releases the activation and A
 //    slots. Each handshake is one elected arrival per warp.
@@ -34,7 +36,6 @@
 
 namespace orch {
 
-constexpr int kSRing = 4;
 constexpr int kWarpProdW = kWarpsDq;              // TMA producer of weights and scales
 constexpr int kWarpProdX = kWarpsDq + 1;          // TMA producer of activations
 constexpr int kWarpMma = kWarpsDq + 2;            // MMA issuer
@@ -54,19 +55,15 @@ struct TcCfg {
   static constexpr uint32_t kTmemCols = kDecode ? 256 : 512;
   static constexpr uint32_t kAccCols = NTILE < 32 ? 32 : NTILE;
   static constexpr int AR = (kTmemCols - kAccCols) / 64 < 4 ? (int)((kTmemCols - kAccCols) / 64) : 4;
-  static constexpr int SW = 6;  // weight ring (<= 6, see below)
+  static constexpr int SW = 6;  // weight ring (with each stage's scales)
   static constexpr int SX = NTILE <= 16 ? 6 : (NTILE <= 32 ? 4 : (NTILE <= 128 ? 3 : 2));
   static constexpr int XSub = NTILE * kSub * 2;  // one 64-k swizzle atom of activations
   static constexpr int XBytes = 2 * XSub;
   static constexpr int OffX = 0;
   static constexpr int OffW = OffX + SX * XBytes;
   static constexpr int OffS = OffW + SW * kWBytes;
-  static constexpr int OffBar = OffS + kSRing * kSBytes;
+  static constexpr int OffBar = OffS + SW * kSBytes;  // a scale slot per weight slot
   static constexpr int Bytes = OffBar + 512;
-  // A scale slot serves the two stages of a 256-k block and is refilled 8 stages later; the
-  // weight producer runs at most SW stages ahead of the dequantisation warps, so SW <= 6
-  // keeps every slot live until both of its stages are read.
-  static_assert(SW <= 6, "scale ring reuse");
   static_assert(2 * SW + 2 * SX + 2 * AR + 1 <= 62, "barrier area");
   // the split-K receive buffer reuses the rings and must stay below the barriers
   static_assert((kTcRows + 16) * NTILE * 4 <= OffBar, "receive buffer");
@@ -221,14 +218,14 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
   if (tid == 0) {
     for (int i = 0; i < C::SW; ++i) {
       mbar_init(&fullW[i], 1);
-      mbar_init(&emptyW[i], kWarpsDq);  // one elected lane per dequantisation warp
+      mbar_init(&emptyW[i], kWarpsDq / 2);  // one elected lane per warp of the stage's group
     }
     for (int i = 0; i < C::SX; ++i) {
       mbar_init(&fullX[i], 1);
       mbar_init(&emptyX[i], 1);
     }
     for (int i = 0; i < C::AR; ++i) {
-      mbar_init(&afull[i], kWarpsDq);
+      mbar_init(&afull[i], kWarpsDq / 2);
       mbar_init(&aempty[i], 1);
     }
     mbar_init(done, 1);
@@ -256,16 +253,20 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
           *failed = 1;
           break;
         }
-        const bool with_s = (p & 1) == 0;
-        mbar_expect_tx(&fullW[v], (uint32_t)(kWBytes + (with_s ? kSBytes : 0)));
+        // Every stage brings its own scales into the scale slot beside its weight slot, under
+        // the same full / empty barriers: the tiled layout's half of the block's [8 groups][128
+        // rows] scales (1 KB), or the reference layout's [128 rows][8 groups] box of the block
+        // (its x, a multiple of 8 fp16, keeps the copy 16-byte aligned).
+        const int half = (st0 + p) & 1;
+        mbar_expect_tx(&fullW[v], (uint32_t)(kWBytes + (LAY == 1 ? kSBytes / 2 : kSBytes)));
         if (LAY == 1) {
           const uint8_t* blk = a0.w + ((size_t)blockIdx.x * nblk + ((st0 + p) >> 1)) * kQ4tBlockBytes;
-          bulk_load(sW + v * kWBytes, blk + ((st0 + p) & 1) * kWBytes, kWBytes, &fullW[v]);
-          if (with_s) bulk_load(sS + ((p >> 1) % kSRing) * kSBytes, blk + 4 * kQ4tStageBytes, kSBytes, &fullW[v]);
+          bulk_load(sW + v * kWBytes, blk + half * kWBytes, kWBytes, &fullW[v]);
+          bulk_load(sS + v * kSBytes, blk + 4 * kQ4tStageBytes + half * (kSBytes / 2), kSBytes / 2, &fullW[v]);
         } else {
           const int k0 = (st0 + p) * kTcBK;
           tma_load_2d(sW + v * kWBytes, &tmw, &fullW[v], k0 >> 1, R0);
-          if (with_s) tma_load_2d(sS + ((p >> 1) % kSRing) * kSBytes, &tms, &fullW[v], k0 >> 5, R0);
+          tma_load_2d(sS + v * kSBytes, &tms, &fullW[v], ((st0 + p) >> 1) * 8, R0);
         }
         issued = p + 1;
       }
@@ -324,12 +325,13 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
     __syncwarp();
   } else {
     // ------- dequantisation warps: packed tile -> fp16 A tile in tensor memory -------
-    // Warp w owns TMEM lanes 32 (w % 4) .. + 31 (= weight rows); warps 0-3 write k 0..63 of
-    // each stage (columns 0..31 of the slot), warps 4-7 k 64..127 (columns 32..63).
+    // Warp w owns TMEM lanes 32 (w % 4) .. + 31 (= weight rows); warps 0-3 take the even
+    // stages and warps 4-7 the odd ones, each warp writing all 128 k of its rows (columns
+    // 0..63 of the slot) in two 64-k halves.
     pdl_wait();
-    const int j2 = warp >> 2, r = (warp & 3) * 32 + lane;
+    const int grp = warp >> 2, r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    for (int s = 0; s < nst; ++s) {
+    for (int s = grp; s < nst; s += 2) {
       const int v = s % C::SW, ai = s % C::AR;
       bool ok = mbar_wait_f(&fullW[v], (uint32_t)(s / C::SW) & 1, failed);
       if (ok && s >= C::AR) ok = mbar_wait_f(&aempty[ai], (uint32_t)(s / C::AR - 1) & 1, failed);
@@ -338,35 +340,47 @@ __global__ void __launch_bounds__(kTcThreads2, TcCfg<NTILE>::kMinBlocks)
         break;
       }
       const uint8_t* wt = sW + v * kWBytes;
-      const __half* st = reinterpret_cast<const __half*>(sS + ((s >> 1) % kSRing) * kSBytes);
-      const int g0 = ((s & 1) * 2 + j2) * 2;  // scale group of this warp's first 32 k in the block
-      uint4 wa, wb;
-      uint32_t sca, scb;
-      if (LAY == 1) {  // 64-k stages [2 halves][128 rows][16 B]; scales [8 groups][128 rows]
-        wa = *reinterpret_cast<const uint4*>(wt + j2 * kQ4tStageBytes + r * 16);
-        wb = *reinterpret_cast<const uint4*>(wt + j2 * kQ4tStageBytes + (kQ4tStageBytes / 2) + r * 16);
-        sca = h2_bits(__half2half2(st[g0 * kTcRows + r]));
-        scb = h2_bits(__half2half2(st[(g0 + 1) * kTcRows + r]));
-      } else {  // TMA boxes: [128 rows][64 B], scales [128 rows][8 groups]
-        wa = *reinterpret_cast<const uint4*>(wt + r * 64 + j2 * 32);
-        wb = *reinterpret_cast<const uint4*>(wt + r * 64 + j2 * 32 + 16);
-        sca = h2_bits(__half2half2(st[r * 8 + g0]));
-        scb = h2_bits(__half2half2(st[r * 8 + g0 + 1]));
+      const __half* st = reinterpret_cast<const __half*>(sS + v * kSBytes);
+      uint4 wa[2], wb[2];
+      uint32_t sca[2], scb[2];
+#pragma unroll
+      for (int j2 = 0; j2 < 2; ++j2) {
+        if (LAY == 1) {  // 64-k stages [2 halves][128 rows][16 B]; the stage's scales [4 groups][128 rows]
+          wa[j2] = *reinterpret_cast<const uint4*>(wt + j2 * kQ4tStageBytes + r * 16);
+          wb[j2] = *reinterpret_cast<const uint4*>(wt + j2 * kQ4tStageBytes + (kQ4tStageBytes / 2) + r * 16);
+          sca[j2] = h2_bits(__half2half2(st[(2 * j2) * kTcRows + r]));
+          scb[j2] = h2_bits(__half2half2(st[(2 * j2 + 1) * kTcRows + r]));
+        } else {  // TMA boxes: [128 rows][64 B], the block's scales [128 rows][8 groups]
+          const int g0 = ((s & 1) * 2 + j2) * 2;  // group of the half's first 32 k in the block
+          wa[j2] = *reinterpret_cast<const uint4*>(wt + r * 64 + j2 * 32);
+          wb[j2] = *reinterpret_cast<const uint4*>(wt + r * 64 + j2 * 32 + 16);
+          sca[j2] = h2_bits(__half2half2(st[r * 8 + g0]));
+          scb[j2] = h2_bits(__half2half2(st[r * 8 + g0 + 1]));
+        }
       }
+      // The slot is refilled by TMA, i.e. written through the async proxy: order this warp's
+      // generic-proxy reads of it before that write. Without the fence, 2-D TMA refills of
+      // reference-layout slots overwrote data still being read, once stages alternated
+      // between the two groups.
+      fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
-      const uint32_t wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-      uint32_t q[32];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t sc = i < 4 ? sca : scb;
-        const uint4 o = LAY == 1 ? dq8_tiled(wv[i], sc) : dq8_natural(wv[i], sc);
-        q[4 * i] = o.x;
-        q[4 * i + 1] = o.y;
-        q[4 * i + 2] = o.z;
-        q[4 * i + 3] = o.w;
+      for (int j2 = 0; j2 < 2; ++j2) {
+        const uint32_t wv[8] = {wa[j2].x, wa[j2].y, wa[j2].z, wa[j2].w, wb[j2].x, wb[j2].y, wb[j2].z, wb[j2].w};
+        uint32_t q[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t sc = i < 4 ? sca[j2] : scb[j2];
+          const uint4 o = LAY == 1 ? dq8_tiled(wv[i], sc) : dq8_natural(wv[i], sc);
+          q[4 * i] = o.x;
+          q[4 * i + 1] = o.y;
+          q[4 * i + 2] = o.z;
+          q[4 * i + 3] = o.w;
+        }
+        // the store's source registers stay live until its wait (tmem_st32 waits)
+        tmem_st32(tmem_a + lane_base + ai * 64 + j2 * 32, q);
       }
-      tmem_st32(tmem_a + lane_base + ai * 64 + j2 * 32, q);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[ai]);

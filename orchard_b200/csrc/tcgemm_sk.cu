@@ -257,6 +257,7 @@ __global__ void __launch_bounds__(kSkThreads, kSkCtasPerSm)
         w4[i] = *reinterpret_cast<const uint4*>(wt + (i >> 1) * kQ4tStageBytes + (i & 1) * (kQ4tStageBytes / 2) + r * 16);
         sc[i] = h2_bits(__half2half2(st[(g0 + i) * kTcRows + r]));
       }
+      fence_proxy_async();  // generic reads of the slot before its async-proxy (bulk copy) refill
       __syncwarp();
       if (lane == 0) mbar_arrive(&emptyW[v]);  // the packed slot is in registers now
 #pragma unroll
