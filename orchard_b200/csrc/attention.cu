@@ -205,6 +205,26 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
   __shared__ float red[32];
   const int d = threadIdx.x;
   const float* wp = a.ws + (size_t)mh * a.S * (HD + 2);
+  if (a.S <= 32) {
+    // Up to 32 splits (batch 1 at the 7B shape has 19): every load is issued before the two
+    // block reductions, so the kernel waits on L2 once instead of once per pass. The sums are
+    // those of the general loop below (split d's weight by thread d, partials in split order).
+    float pv[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pv[j] = j < a.S ? wp[j * (HD + 2) + 2 + d] : 0.f;
+    const float ms = d < a.S ? wp[d * (HD + 2)] : -INFINITY;
+    const float ls = d < a.S ? wp[d * (HD + 2) + 1] : 0.f;
+    const float gmax = block_max(ms, red);
+    const float f = ms == -INFINITY ? 0.f : __expf(ms - gmax);
+    fsh[d] = f;
+    const float den = block_sum(fmaf(f, ls, 0.f), red);  // its barriers also publish fsh
+    float num = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < a.S) num = fmaf(fsh[j], pv[j], num);
+    a.out[(size_t)m * a.nh * HD + h * HD + d] = __float2half_rn(num / den);
+    return;
+  }
   float lmax = -INFINITY;
   for (int s = d; s < a.S; s += HD) lmax = fmaxf(lmax, wp[s * (HD + 2)]);
   const float gmax = block_max(lmax, red);
