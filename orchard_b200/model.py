@@ -3,17 +3,20 @@
 Reference API: ``orchard.Llama(model_path)``, ``load_lora``, ``generate_batch(prompts,
 max_tokens=50, temperature=0.7)`` (orchard/model.py:197-381). Arithmetic follows
 ``LlamaLayer.forward`` (orchard/model.py:78-195); the per-layer sequence of the
-reference's ~14 synchronous ops plus host attention becomes five launches:
+reference's ~14 synchronous ops plus host attention becomes seven launches:
 
   1. RMSNorm (fp32 residual -> fp16)                          rmsnorm.metal
   2. Q/K/V INT4 projection + LoRA + RoPE + KV-cache append     model.py:94-124
-  3. attention over the device KV cache                        model.py:117-137
+  3. attention over the device KV cache (+ a combine launch when positions are split)
+                                                               model.py:117-137
   4. O INT4 projection + LoRA + residual add                   model.py:147-157
   5. RMSNorm, gate/up INT4 projection + LoRA + SwiGLU, down projection + residual
      (three launches)                                          model.py:160-193
 
-then final RMSNorm, the INT4 lm_head and a row argmax. A whole decode step for a batch
-size is captured once in a CUDA graph and replayed.
+At 1-8 rows, on projections without a LoRA term, each RMSNorm is folded into the GEMV that
+follows it (the GEMV normalises the fp32 residual itself), leaving five. Then come the final
+RMSNorm, the INT4 lm_head and a row argmax. A whole decode step for a batch size is
+captured once in a CUDA graph and replayed.
 
 Token flow of ``generate_batch`` is the reference's: prompts are prefilled one position
 at a time (all sequences of the batch together), the last prompt token is fed again as
