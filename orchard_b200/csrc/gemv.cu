@@ -91,6 +91,11 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tiled_kernel(const QArgs a) {
     cp_async_commit();  // empty groups keep the group count uniform
   };
 
+  // A CTA may write a cluster peer's shared memory only once the peer runs. With the RMSNorm
+  // prologue its cluster barrier establishes that; otherwise a split barrier does, arrived
+  // here and waited on just before the push, when it has long completed.
+  const bool norm_prologue = a.norm_w != nullptr;
+  if (!norm_prologue) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   // Weights do not depend on the previous kernel (the packers release dependents only on
   // exit): start the rings before griddepcontrol.wait.
   issue(0);
@@ -224,10 +229,15 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tiled_kernel(const QArgs a) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] += acc2[i];
 
-  // ---- partials -> owners' receive buffers (they alias the rings and x) ----
+  // ---- partials -> owners' receive buffers ----
+  // The receive buffer has its own region past the rings and the largest K slice's
+  // activations (the same offset in every CTA of the cluster), so partials are pushed as soon
+  // as this CTA's loop ends: one cluster barrier, in qgemm_finish. (Aliased onto the rings it
+  // needed a barrier before the push as well: 0.8 us of a ~4 us launch at one row.)
   cg::cluster_group cl = cg::this_cluster();
-  cl.sync();
-  float* recv = reinterpret_cast<float*>(smem);
+  if (!norm_prologue) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  const int nb_max = (nblk + KS - 1) / KS;
+  float* recv = reinterpret_cast<float*>(smem + kGvRingBytes + (size_t)a.M * gv_xpitch(4 * nb_max));
   const int Mp = epi_mp(a.M);
   const int n0 = 2 * c;
   if (n0 < Mp) {  // Mp is a multiple of 4, so n0 + 1 < Mp too
@@ -244,10 +254,8 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tiled_kernel(const QArgs a) {
 }
 
 template <int EPI>
-size_t gv_smem(int M, int nst) {
-  const size_t ring = (size_t)kGvRingBytes + (size_t)M * gv_xpitch(nst);
-  const size_t red = (size_t)4 * epi_recv_floats<kGvRows>(M);
-  return std::max(ring, red);
+size_t gv_smem(int M, int nst) {  // rings, activations of the largest K slice, receive buffer
+  return (size_t)kGvRingBytes + (size_t)M * gv_xpitch(nst) + (size_t)4 * epi_recv_floats<kGvRows>(M);
 }
 
 }  // namespace
