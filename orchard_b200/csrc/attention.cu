@@ -126,6 +126,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       lmax = fmaxf(lmax, s1);
     }
   }
+  // pass 2's geometry: LPR lanes cover one position row in 16-byte pieces, so a warp load
+  // instruction reads RPW whole rows; U such loads per lane are in flight before any is used
+  constexpr int LPR = HD / 8, RPW = 32 / LPR, NW = kAttnThreads / 32, STR = NW * RPW, U = 8;
+  const int vsub = lane / LPR, ci = lane - vsub * LPR;
+  // A split that fits one batch of U loads per lane (the short splits of small batches):
+  // its V rows are requested now, so their latency runs under the softmax reductions.
+  const bool one_batch = p1 - p0 <= U * STR;  // uniform per CTA
+  const int tv = p0 + warp * RPW + vsub;
+  uint4 rawv[U];
+  if (one_batch) {
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      rawv[u] = tv + u * STR < p1 ? ld_stream16(V + (size_t)(tv + u * STR) * HD + ci * 8) : make_uint4(0, 0, 0, 0);
+  }
   const float mx = block_max(lmax, red);
   float lsum = 0.f;
   for (int t = threadIdx.x; t < p1 - p0; t += kAttnThreads) {
@@ -135,10 +149,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   }
   const float sum = block_sum(lsum, red);  // contains __syncthreads: sc[] complete
 
-  // pass 2: LPR lanes cover one position row in 16-byte pieces, so a warp load instruction
-  // reads RPW whole rows; U such loads per lane are in flight before any is used
-  constexpr int LPR = HD / 8, RPW = 32 / LPR, NW = kAttnThreads / 32, STR = NW * RPW, U = 8;
-  const int vsub = lane / LPR, ci = lane - vsub * LPR;
+  // pass 2: P.V in ascending position order per lane
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -154,15 +165,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     acc[6] = fmaf(w, f3.x, acc[6]);
     acc[7] = fmaf(w, f3.y, acc[7]);
   };
-  int t = p0 + warp * RPW + vsub;
-  for (; t + (U - 1) * STR < p1; t += U * STR) {
-    uint4 raw[U];
+  if (one_batch) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) raw[u] = ld_stream16(V + (size_t)(t + u * STR) * HD + ci * 8);
+    for (int u = 0; u < U; ++u)
+      if (tv + u * STR < p1) fma8(rawv[u], sc[tv + u * STR - p0]);
+  } else {
+    int t = tv;
+    for (; t + (U - 1) * STR < p1; t += U * STR) {
+      uint4 raw[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) fma8(raw[u], sc[t + u * STR - p0]);
+      for (int u = 0; u < U; ++u) raw[u] = ld_stream16(V + (size_t)(t + u * STR) * HD + ci * 8);
+#pragma unroll
+      for (int u = 0; u < U; ++u) fma8(raw[u], sc[t + u * STR - p0]);
+    }
+    for (; t < p1; t += STR) fma8(ld_stream16(V + (size_t)t * HD + ci * 8), sc[t - p0]);
   }
-  for (; t < p1; t += STR) fma8(ld_stream16(V + (size_t)t * HD + ci * 8), sc[t - p0]);
 #pragma unroll
   for (int o = LPR; o < 32; o <<= 1)
 #pragma unroll
@@ -306,9 +323,26 @@ __global__ void argmax_rows_kernel(const float* logits, int V, int* out, float2*
   const float* r = logits + (size_t)blockIdx.x * V;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+  // Eight loads in flight per step, compared in ascending index order as one at a time would
+  // (a dependent load per element was 31 L2 round trips: 18 us for one 32000-entry row).
+  int i = threadIdx.x;
+  const int step = blockDim.x;
+  for (; i + 7 * step < V; i += 8 * step) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = r[i + u * step];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = i + u * step;
+      if (v[u] > best || (v[u] == best && j < bi) || (v[u] != v[u] && best == best)) {  // NaN wins, as np.argmax
+        best = v[u];
+        bi = j;
+      }
+    }
+  }
+  for (; i < V; i += step) {
     const float v = r[i];
-    if (v > best || (v == best && i < bi) || (v != v && best == best)) {  // NaN wins, as np.argmax
+    if (v > best || (v == best && i < bi) || (v != v && best == best)) {
       best = v;
       bi = i;
     }

@@ -571,6 +571,12 @@ int tc_qgemm_run(QArgs a, cudaStream_t st) {
   const int slots = (ntile <= 64 ? 2 : 1) * num_sms();  // TcCfg::kMinBlocks
   int KS = 1;
   while (KS < 8 && tiles * KS * 2 <= slots && nblk >= KS * 4) KS *= 2;
+  static const int ks_force = [] {  // ORCHARD_TC_KS=1/2/4/8 fixes the split (measurements)
+    const char* e = std::getenv("ORCHARD_TC_KS");
+    const int v = e ? std::atoi(e) : 0;
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+  }();
+  if (ks_force > 0) KS = std::min(ks_force, std::max(1, nblk));
   const int rc = tiled ? tc_dispatch<EPI, 1>(mx, mw, ms, a, ntile, KS, st)
                        : tc_dispatch<EPI, 0>(mx, mw, ms, a, ntile, KS, st);
   if (rc != ORCH_OK) return rc;
