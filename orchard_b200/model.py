@@ -689,10 +689,10 @@ class Llama:
         """Token ids in, token ids out; the reference's generate_batch token flow.
 
         Every decode step copies that step's positions host->device (pinned) and the sampled
-        tokens device->host. With temperature 0 the next step is enqueued before the host
-        reads the previous step's tokens, so the GPU never waits on the host; a row that
-        produced EOS keeps computing (its later tokens are dropped), which leaves the other
-        rows' results unchanged. With temperature > 0 the softmax and the draw run on the
+        tokens device->host. With temperature 0 the host reads a step's tokens two steps
+        later, so one step is always queued behind the running one and the GPU never waits on
+        the host; a row that produced EOS keeps computing for up to two steps (those tokens
+        are dropped), which leaves every row's result unchanged. With temperature > 0 the softmax and the draw run on the
         device too: the host draws one uniform per active row from the global NumPy RNG, in
         row order (the draws np.random.choice makes in the reference), and copies them in
         with the positions. ``stats`` (optional dict) receives the prefill and decode
@@ -731,10 +731,13 @@ class Llama:
                 if not ignore_eos and nxt[b] == EOS_ID:
                     active[b] = False
 
+        LAG = 2  # greedy: steps enqueued ahead of the host's reading of their tokens
         steps = 0
+        consumed = 0
         for step in range(max_tokens):
-            if greedy and step >= 1:
-                consume(step - 1)
+            if greedy and step >= LAG:
+                consume(step - LAG)
+                consumed = step - LAG + 1
             if not active.any() and eng.split is None:  # split ranks stay in step together
                 break
             eng.pos[:B].copy_(pos_host[step], non_blocking=True)
@@ -763,8 +766,11 @@ class Llama:
                         active[b] = False
                 eng.tok_in[:B].copy_(eng.tok_out[:B])
             steps += 1
-        if greedy and steps > 0 and len(events) == steps and active.any():
-            consume(steps - 1)
+        if greedy:
+            for st in range(consumed, steps):
+                if not active.any():
+                    break
+                consume(st)
         torch.cuda.synchronize(eng.device)
         t2 = time.perf_counter()
         if stats is not None:
