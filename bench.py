@@ -108,7 +108,7 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------
 # model construction (random init on the device, packed with the reference rule)
 # ------------------------------------------------------------------------------------------------
-def build_model(cfg, device, max_batch, seed=1234, group=None):
+def build_model(cfg, device, max_batch, seed=1234, group=None, split_heads=False):
     import torch
 
     from orchard_b200 import loader
@@ -134,7 +134,8 @@ def build_model(cfg, device, max_batch, seed=1234, group=None):
     ck.embed = torch.randn((V, H), generator=gen, device=device).half()
     ck.norm = (1 + 0.1 * torch.randn(H, generator=gen, device=device)).half().float().cpu().numpy()
     ck.lm_head = packed(V, H)
-    return Llama(checkpoint=ck, device=device, max_batch=max_batch, max_seq=MAX_SEQ, group=group)
+    return Llama(checkpoint=ck, device=device, max_batch=max_batch, max_seq=MAX_SEQ, group=group,
+                 split_heads=split_heads)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -354,44 +355,108 @@ def time_column_split(cfg, dev, global_batch, steps, warmup, rank, world, check_
         v0, v1, tin, tout, lgs = check
         ref = build_model(cfg, dev, B, seed=4321)  # unsplit, same weights
         ref.prefill(prompts)
-        re = ref.engine
-        match, total, err, clear, clear_match, tie_ok = 0, 0, 0.0, 0, 0, 0
-        for s in range(check_steps):
-            re.pos[:B].fill_(PROMPT + s)
-            re.tok_in[:B].copy_(tin[s])
-            re.step(B, logits=True, graph=False)
-            same = re.tok_out[:B] == tout[s]
-            match += int(same.sum().item())
-            total += B
-            full = re.logits[:B, v0:v1]
-            err = max(err, float((lgs[s] - full).abs().max().item() / max(full.abs().max().item(), 1e-30)))
-            # a row whose two best logits are more than 1e-2 of max |logit| apart must pick the
-            # same token; closer rows may differ by summation order, but the split's pick must
-            # then be within that margin of the best logit
-            lg = re.logits[:B]
-            tol = 1e-2 * lg.abs().amax(dim=1)
-            top2 = torch.topk(lg, 2, dim=1).values
-            is_clear = (top2[:, 0] - top2[:, 1]) > tol
-            clear += int(is_clear.sum().item())
-            clear_match += int((same & is_clear).sum().item())
-            picked = lg.gather(1, tout[s].long().view(-1, 1)).view(-1)
-            tie_ok += int(((~same) & ~is_clear & (top2[:, 0] - picked <= tol)).sum().item())
-        del ref, re
+        out["check"] = split_check(ref.engine, prompts, tin, tout, lgs, v0, v1, B, dev)
+        del ref
         torch.cuda.empty_cache()
-        st = torch.tensor([match, total, clear, clear_match, tie_ok], dtype=torch.float64, device=dev)
-        dist.all_reduce(st)
-        e = torch.tensor([err], device=dev)
-        dist.all_reduce(e, op=dist.ReduceOp.MAX)
-        m, n, c, cm, ok = (int(v) for v in st.tolist())
-        out["check"] = {"steps": check_steps,
-                        "tokens_match": bool(cm == c and m + ok == n and e.item() <= 1e-2),
-                        "tokens_matched": f"{m}/{n}", "clear_rows_matched": f"{cm}/{c}",
-                        "other_rows_within_tie_margin": f"{ok}/{n - c}",
-                        "logits_max_rel": float(e.item()),
-                        "rule": "rows with a top-2 gap > 1e-2 of max|logit| pick the same token; the rest pick a "
-                                "token within that margin of the best; logits of each rank's vocabulary slice "
-                                "within 1e-2 (max|split - unsplit| / max|unsplit|)",
-                        "against": "unsplit engine, same weights, prompts and input tokens"}
+    return out
+
+
+def split_check(eng_ref, prompts, tin, tout, lgs, v0, v1, rows, dev):
+    """Decode steps of an unsplit engine on the inputs a split engine saw (`tin`, one tensor of
+    input tokens per step) against the split's tokens `tout` and its vocabulary slice of the
+    logits `lgs` (rows [0, rows) of both); summed over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    match, total, err, clear, clear_match, tie_ok = 0, 0, 0.0, 0, 0, 0
+    for s in range(len(tin)):
+        eng_ref.pos[:rows].fill_(PROMPT + s)
+        eng_ref.tok_in[:rows].copy_(tin[s])
+        eng_ref.step(rows, logits=True, graph=False)
+        same = eng_ref.tok_out[:rows] == tout[s]
+        match += int(same.sum().item())
+        total += rows
+        full = eng_ref.logits[:rows, v0:v1]
+        err = max(err, float((lgs[s] - full).abs().max().item() / max(full.abs().max().item(), 1e-30)))
+        # a row whose two best logits are more than 1e-2 of max |logit| apart must pick the
+        # same token; closer rows may differ by summation order, but the split's pick must
+        # then be within that margin of the best logit
+        lg = eng_ref.logits[:rows]
+        tol = 1e-2 * lg.abs().amax(dim=1)
+        top2 = torch.topk(lg, 2, dim=1).values
+        is_clear = (top2[:, 0] - top2[:, 1]) > tol
+        clear += int(is_clear.sum().item())
+        clear_match += int((same & is_clear).sum().item())
+        picked = lg.gather(1, tout[s].long().view(-1, 1)).view(-1)
+        tie_ok += int(((~same) & ~is_clear & (top2[:, 0] - picked <= tol)).sum().item())
+    st = torch.tensor([match, total, clear, clear_match, tie_ok], dtype=torch.float64, device=dev)
+    dist.all_reduce(st)
+    e = torch.tensor([err], device=dev)
+    dist.all_reduce(e, op=dist.ReduceOp.MAX)
+    m, n, c, cm, ok = (int(v) for v in st.tolist())
+    return {"steps": len(tin),
+            "tokens_match": bool(cm == c and m + ok == n and e.item() <= 1e-2),
+            "tokens_matched": f"{m}/{n}", "clear_rows_matched": f"{cm}/{c}",
+            "other_rows_within_tie_margin": f"{ok}/{n - c}",
+            "logits_max_rel": float(e.item()),
+            "rule": "rows with a top-2 gap > 1e-2 of max|logit| pick the same token; the rest pick a "
+                    "token within that margin of the best; logits of each rank's vocabulary slice "
+                    "within 1e-2 (max|split - unsplit| / max|unsplit|)",
+            "against": "unsplit engine, same weights, prompts and input tokens"}
+
+
+def time_head_split(cfg, dev, batches, steps, warmup, world, check_steps=8):
+    """The head split (every rank runs all sequences; attention heads, FFN and vocabulary
+    divided over the ranks; two all-reduces of the residual per layer): for each global
+    batch in `batches` (one engine sized for the largest), greedy decode steps timed on the
+    device (max over ranks). Before timing the largest batch, `check_steps` eager steps are
+    compared with the unsplit engine on the same weights, prompts and input tokens."""
+    import torch
+    import torch.distributed as dist
+
+    Bmax = max(batches)
+    llm = build_model(cfg, dev, Bmax, seed=4321, group=dist.group.WORLD, split_heads=True)
+    eng = llm.engine
+    g = np.random.default_rng([20261201, 7, 0])  # the same prompts on every rank
+    prompts = g.integers(0, cfg["vocab_size"], (Bmax, PROMPT)).tolist()
+    llm.prefill(prompts)
+    sp = eng.split
+    out = {"heads_per_rank": sp.h_local, "by_global_batch": {}}
+    check = None
+    if check_steps:
+        last = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)
+        eng.tok_in[:Bmax].copy_(last)
+        tin, tout, lgs = [], [], []
+        for s in range(check_steps):
+            eng.pos[:Bmax].fill_(PROMPT + s)
+            tin.append(eng.tok_in[:Bmax].clone())
+            eng.step(Bmax, logits=True, graph=False)
+            tout.append(eng.tok_out[:Bmax].clone())
+            lgs.append(eng.sdec.logits[:Bmax].clone())
+            eng.tok_in[:Bmax].copy_(eng.tok_out[:Bmax])
+        check = (tin, tout, lgs)
+    start = PROMPT + 3 - warmup if warmup <= 3 else PROMPT
+    for B in sorted(batches, reverse=True):
+        eng.pos[:B].fill_(PROMPT)
+        eng.step(B, logits=True)  # capture the graph (with its NCCL calls) before timing
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        secs = time_decode(llm, B, steps, warmup, start)
+        t = torch.tensor([secs], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+        out["by_global_batch"][str(B)] = {"tok_s": round(B * steps / secs, 2),
+                                          "ms_per_step": round(secs / steps * 1000, 4), "steps": steps}
+    v0, v1 = sp.v0, sp.v1
+    eng.release_graphs()
+    del llm, eng
+    torch.cuda.empty_cache()
+    if check is not None:
+        ref = build_model(cfg, dev, Bmax, seed=4321)  # unsplit, same weights
+        ref.prefill(prompts)
+        out["check"] = split_check(ref.engine, prompts, *check, v0, v1, Bmax, dev)
+        del ref
+        torch.cuda.empty_cache()
     return out
 
 
@@ -584,6 +649,14 @@ def run_ours(args):
         line["column_split"] = {"note": "FFN and lm_head column-split over NCCL; attention data-parallel "
                                         "(replicated attention weights); two collectives per layer",
                                 "by_global_batch": splits}
+        try:  # a failure here (the same on every rank) must not cost the line
+            hs = time_head_split(cfg, dev, sorted({B, 1}), min(args.steps, 32), args.warmup, world)
+            hs["note"] = ("attention heads (Q/K/V rows, O columns, KV cache), FFN and lm_head split over NCCL; "
+                          "every rank runs all sequences; two all-reduces of the fp32 residual per layer")
+        except Exception as e:
+            hs = {"error": repr(e)[:300]}
+            torch.cuda.empty_cache()
+        line["head_split"] = hs
         llm = build_model(cfg, dev, max_b, seed=1234 + rank)
         eng = llm.engine
         llm.prefill(prompts)

@@ -38,7 +38,8 @@ import torch
 from . import _lib
 from ._lib import F16, F32, call, ptr
 from .loader import Checkpoint, from_tensors, load_checkpoint, load_lora
-from .parallel import ColumnSplit, ffn_column_split, head_column_split
+from .parallel import (ColumnSplit, attention_head_split, ffn_column_split, ffn_head_split, head_column_split,
+                       vocab_head_split)
 
 EOS_ID = 2
 
@@ -175,6 +176,12 @@ class DeviceLayer:
             w1, s1, w3, s3, w2, s2 = split.ffn_shard(*q["w1"], *q["w3"], *q["w2"])
             q["w1"], q["w3"], q["w2"] = (w1, s1), (w3, s3), (w2.contiguous(), s2.contiguous())
             F = split.f_local
+        Ha = H  # width of this rank's Q (= K = V) rows and of the O projection's K
+        if split is not None and split.heads:  # this rank's heads: Q/K/V rows, O columns
+            wq, sq, wk, sk, wv, sv, wo, so = split.attn_shard(*q["wq"], *q["wk"], *q["wv"], *q["wo"], cfg.head_dim)
+            q["wq"], q["wk"], q["wv"] = (wq, sq), (wk, sk), (wv, sv)
+            q["wo"] = (wo.contiguous(), so.contiguous())
+            Ha = split.h_local * cfg.head_dim
         self.wqkv = torch.cat([q["wq"][0], q["wk"][0], q["wv"][0]]).contiguous()
         self.sqkv = torch.cat([q["wq"][1], q["wk"][1], q["wv"][1]]).contiguous()
         self.wo, self.so = q["wo"]
@@ -183,9 +190,10 @@ class DeviceLayer:
         del q
         self.attn_norm = torch.as_tensor(np.asarray(entries["attn_norm"], np.float32)).to(device)
         self.ffn_norm = torch.as_tensor(np.asarray(entries["ffn_norm"], np.float32)).to(device)
-        assert self.wqkv.shape == (3 * H, H // 2) and self.w13.shape == (2 * F, H // 2)
-        assert self.w2.shape == (H, F // 2)
+        assert self.wqkv.shape == (3 * Ha, H // 2) and self.w13.shape == (2 * F, H // 2)
+        assert self.w2.shape == (H, F // 2) and self.wo.shape == (H, Ha // 2)
         self.f_local = F
+        self.h_attn = Ha
         self.tiled = tiled
         if tiled:
             self.tqkv = tile_q4(self.wqkv, self.sqkv)
@@ -230,7 +238,7 @@ class RowBuffers:
     outputs, per-row token / position / cache slot, LoRA x.A rows and the attention
     workspace."""
 
-    def __init__(self, rows: int, cfg: "LlamaConfig", max_seq: int, device, logits: bool):
+    def __init__(self, rows: int, cfg: "LlamaConfig", max_seq: int, device, logits: bool, heads: int = 0):
         H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
         nh, hd = cfg.num_attention_heads, cfg.head_dim
         self.rows = rows
@@ -248,7 +256,8 @@ class RowBuffers:
         self.lora_t = torch.zeros((rows, 3 * 64), dtype=torch.float32, device=device)
         lib = _lib.lib()
         ms = list(range(1, min(rows, 256) + 1)) + [rows]  # splits only happen for few rows
-        ws = max(lib.orch_attention_workspace_bytes(m, nh, hd, max_seq) for m in ms)
+        # a rank of the head split runs fewer heads per row (its split count may differ)
+        ws = max(lib.orch_attention_workspace_bytes(m, h, hd, max_seq) for m in ms for h in {nh, heads or nh})
         self.attn_ws = torch.zeros(max(ws, 16) // 4 + 1, dtype=torch.float32, device=device)
         self.attn_ws_bytes = ws
 
@@ -272,11 +281,75 @@ class _SplitBuffers:
         self.pairs_all = torch.zeros((W * W * R, 2), dtype=torch.float32, device=device)
 
 
+class _HeadSplitBuffers:
+    """Buffers of the head split's lm_head for up to ``rb.rows`` rows (every rank holds all
+    rows): the vocabulary slice's logits, this rank's (max, id) pairs and every rank's."""
+
+    def __init__(self, rb: RowBuffers, split: ColumnSplit, device):
+        R = rb.rows
+        self.x, self.xn, self.tok = rb.x, rb.xn, rb.tok_out
+        self.logits = torch.zeros((R, split.v_local), dtype=torch.float32, device=device)
+        self.pairs = torch.zeros((R, 2), dtype=torch.float32, device=device)
+        self.pairs_all = torch.zeros((split.world * R, 2), dtype=torch.float32, device=device)
+
+
+class _LayerCtx:
+    """What the head split's ops need of one layer: its weights, its slice of the KV cache
+    and, for a prefill chunk, the attention work units."""
+
+    def __init__(self, layer: "DeviceLayer", kc: torch.Tensor, vc: torch.Tensor, units: Optional[torch.Tensor]):
+        self.L, self.kc, self.vc, self.units = layer, kc, vc, units
+
+
 class _CudaSplitOps:
-    """The column split's kernels on this rank (parallel.py names the order)."""
+    """The column split's and the head split's kernels on this rank (parallel.py names the
+    order)."""
 
     def __init__(self, eng: "DecodeEngine"):
         self.e = eng
+
+    # -- head split (all rows on every rank, RowBuffers b) --------------------------------
+    def qkv_local(self, ctx, b, rows):
+        e, L, c = self.e, ctx.L, self.e.cfg
+        call("orch_q4t_rms_qkv_rope", ptr(L.tqkv), ptr(b.x), ptr(L.attn_norm), c.rms_norm_eps, ptr(b.xn), rows,
+             c.hidden_size, L.h_attn, e.nh_local, ptr(b.pos), ptr(b.slots), ptr(e.cos), ptr(e.sin), e.max_pos,
+             ptr(b.q), ptr(ctx.kc), ptr(ctx.vc), e.max_seq, e.num_slots, _stream())
+
+    def attention_local(self, ctx, b, rows):
+        e, hd = self.e, self.e.cfg.head_dim
+        if ctx.units is not None:
+            call("orch_attention_prefill", ptr(b.q), ptr(ctx.kc), ptr(ctx.vc), ptr(ctx.units), ctx.units.shape[0],
+                 ptr(b.attn), rows, e.nh_local, hd, e.max_seq, e.num_slots, _stream())
+        else:
+            call("orch_attention_decode", ptr(b.q), ptr(ctx.kc), ptr(ctx.vc), ptr(b.pos), ptr(b.slots),
+                 ptr(b.attn), rows, e.nh_local, hd, e.max_seq, e.num_slots, ptr(b.attn_ws), b.attn_ws_bytes,
+                 _stream())
+
+    def o_partial(self, ctx, b, rows, resid):
+        L, H = ctx.L, self.e.cfg.hidden_size
+        if resid:
+            call("orch_q4t_linear_resid", ptr(L.to), ptr(b.attn), ptr(b.x), rows, L.h_attn, H, None, None, 0,
+                 _stream())
+        else:
+            call("orch_q4t_gemm", ptr(L.to), ptr(b.attn), ptr(b.x), F32, L.h_attn, H, rows, _stream())
+
+    def gate_up_local(self, ctx, b, rows):
+        L, c = ctx.L, self.e.cfg
+        call("orch_q4t_rms_linear_swiglu", ptr(L.t13), ptr(b.x), ptr(L.ffn_norm), c.rms_norm_eps, ptr(b.xn),
+             ptr(b.h), rows, c.hidden_size, L.f_local, _stream())
+
+    def down_partial_resid(self, ctx, b, rows, resid):
+        L, H = ctx.L, self.e.cfg.hidden_size
+        if resid:
+            call("orch_q4t_linear_resid", ptr(L.t2), ptr(b.h), ptr(b.x), rows, L.f_local, H, None, None, 0,
+                 _stream())
+        else:
+            call("orch_q4t_gemm", ptr(L.t2), ptr(b.h), ptr(b.x), F32, L.f_local, H, rows, _stream())
+
+    def merge_all_pairs(self, pairs_all, tok, rows):
+        call("orch_argmax_merge", ptr(pairs_all), self.e.split.world, rows, 0, rows, ptr(tok), _stream())
+
+    # -- column split and shared -----------------------------------------------------------
 
     def rmsnorm(self, x, w, xn, rows):
         c = self.e.cfg
@@ -313,8 +386,12 @@ class _NcclComm:
     """Collectives of the column split over a torch.distributed (NCCL) group; buffers are
     row-major, the first ``rows`` rows of the input and ``world * rows`` of the output."""
 
-    def __init__(self, group, world: int):
-        self.group, self.world = group, world
+    def __init__(self, group, world: int, rank: int):
+        self.group, self.world, self.rank = group, world, rank
+
+    def all_reduce(self, x, rows):
+        import torch.distributed as dist
+        dist.all_reduce(x[:rows], op=dist.ReduceOp.SUM, group=self.group)
 
     def all_gather(self, out, inp, rows):
         import torch.distributed as dist
@@ -329,10 +406,13 @@ class DecodeEngine:
     """Device state for up to ``max_batch`` sequences of up to ``max_seq`` positions.
     With ``group`` (a torch.distributed NCCL group of several ranks, one GPU each) the
     sequences are sharded over the ranks and the FFN and vocabulary projections are split
-    by columns (parallel.py); ``M`` then counts this rank's rows, equal on every rank."""
+    by columns (parallel.py); ``M`` then counts this rank's rows, equal on every rank.
+    With ``group`` and ``split_heads`` every rank runs the same rows (the same prompts and
+    tokens on every rank) and holds a slice of the attention heads (their Q/K/V/O weights
+    and KV cache) beside its FFN and vocabulary columns; ``M`` counts all rows."""
 
     def __init__(self, ck: Checkpoint, device=0, max_batch: int = 32, max_seq: Optional[int] = None,
-                 tiled: bool = True, group=None):
+                 tiled: bool = True, group=None, split_heads: bool = False):
         if not torch.cuda.is_available():
             raise RuntimeError("orchard_b200 needs a CUDA device (there is no CPU fallback)")
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
@@ -357,7 +437,10 @@ class DecodeEngine:
             if world > 1:
                 if not tiled:
                     raise ValueError("the column split runs on tiled weights")
-                self.split = ColumnSplit.plan(F, V, world, rank)
+                if split_heads:
+                    self.split = ColumnSplit.plan(F, V, world, rank, cfg.num_attention_heads, cfg.head_dim)
+                else:
+                    self.split = ColumnSplit.plan(F, V, world, rank)
         self.layers = [DeviceLayer(e, cfg, dev, tiled, self.split) for e in ck.layers]
         emb = ck.embed if isinstance(ck.embed, torch.Tensor) else torch.as_tensor(np.asarray(ck.embed))
         if emb.dtype not in (torch.float16, torch.float32):
@@ -376,24 +459,31 @@ class DecodeEngine:
         self.cos = torch.as_tensor(cos).to(dev)
         self.sin = torch.as_tensor(sin).to(dev)
         nl, nh, hd = cfg.num_hidden_layers, cfg.num_attention_heads, cfg.head_dim
+        self.heads_split = self.split is not None and self.split.heads
+        self.nh_local = self.split.h_local if self.heads_split else nh  # heads in this rank's cache
         # with the column split one extra slot takes the padding rows of a prefill whose
         # token count is below another rank's (their K/V land there and are never read)
-        self.scratch_slot = max_batch if self.split is not None else -1
+        self.columns_split = self.split is not None and not self.heads_split
+        self.scratch_slot = max_batch if self.columns_split else -1
         # prefill attention on the tensor-core kernel (head_dim 128); False: the decode kernel
         # per row (ORCHARD_PREFILL_ATTN=decode)
         self.prefill_attention = os.environ.get("ORCHARD_PREFILL_ATTN", "tc") != "decode"
-        nslots = max_batch + (1 if self.split is not None else 0)
+        nslots = max_batch + (1 if self.columns_split else 0)
         self.num_slots = nslots
-        self.k_cache = torch.zeros((nl, nslots, nh, self.max_seq, hd), dtype=torch.float16, device=dev)
+        self.k_cache = torch.zeros((nl, nslots, self.nh_local, self.max_seq, hd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.lora_r = 0
-        self.dec = RowBuffers(max_batch, cfg, self.max_seq, dev, logits=self.split is None)
+        self.dec = RowBuffers(max_batch, cfg, self.max_seq, dev, logits=self.split is None, heads=self.nh_local)
         self.pre: Optional[RowBuffers] = None
-        self.sdec = _SplitBuffers(self.dec, self.split, cfg, dev) if self.split is not None else None
+        self.sdec = None
+        if self.heads_split:
+            self.sdec = _HeadSplitBuffers(self.dec, self.split, dev)
+        elif self.split is not None:
+            self.sdec = _SplitBuffers(self.dec, self.split, cfg, dev)
         self.spre: Optional[_SplitBuffers] = None
         if self.split is not None:
             self._split_ops = _CudaSplitOps(self)
-            self._comm = _NcclComm(group, self.split.world)
+            self._comm = _NcclComm(group, self.split.world, self.split.rank)
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         torch.cuda.synchronize(dev)
 
@@ -410,6 +500,8 @@ class DecodeEngine:
     def set_lora(self, per_layer: Dict[int, Dict[str, tuple]], r: int):
         if r > 64:
             raise ValueError("LoRA rank above 64 is not supported by the fused epilogues")
+        if self.heads_split and any(per_layer.values()):
+            raise ValueError("LoRA adapters are not supported with the head split")
         for li, layer in enumerate(self.layers):
             layer.set_lora(per_layer.get(li, {}), self.cfg, r, self.device)
         self.lora_r = r
@@ -445,6 +537,11 @@ class DecodeEngine:
         nh, hd, eps = cfg.num_attention_heads, cfg.head_dim, cfg.rms_norm_eps
         L = self.layers[li]
         kc, vc = self.k_cache[li], self.v_cache[li]
+        if self.heads_split:  # all rows here, this rank's heads and FFN columns (parallel.py)
+            ctx = _LayerCtx(L, kc, vc, units)
+            attention_head_split(self._split_ops, self._comm, ctx, b, M)
+            ffn_head_split(self._split_ops, self._comm, ctx, b, M)
+            return
         if L.tiled and "qkv" not in L.lora:
             # RMSNorm fused in front of the projection (one launch for up to 8 rows)
             call("orch_q4t_rms_qkv_rope", ptr(L.tqkv), ptr(b.x), ptr(L.attn_norm), eps, ptr(b.xn), M, H, H, nh,
@@ -503,6 +600,9 @@ class DecodeEngine:
         b = self.dec
         cfg, s = self.cfg, _stream()
         H, V = cfg.hidden_size, cfg.vocab_size
+        if self.heads_split:
+            vocab_head_split(self._split_ops, self._comm, self.sdec, M)
+            return
         if self.split is not None:
             head_column_split(self._split_ops, self._comm, self.sdec, M)
             return
@@ -526,9 +626,11 @@ class DecodeEngine:
         if self.split is not None:
             # every rank runs the same chunks (the FFN collectives): pad to the largest count
             import torch.distributed as dist
-            cnt = torch.tensor([n], dtype=torch.int64, device=self.device)
+            cnt = torch.tensor([n, -n], dtype=torch.int64, device=self.device)
             dist.all_reduce(cnt, op=dist.ReduceOp.MAX, group=self.group)
-            pad = int(cnt.item()) - n
+            pad = int(cnt[0].item()) - n
+            if self.heads_split and (pad or int(cnt[1].item()) != -n):
+                raise ValueError("the head split runs the same rows on every rank: token counts differ")
             if pad:
                 tokens = np.concatenate([np.asarray(tokens, np.int32), np.zeros(pad, np.int32)])
                 positions = np.concatenate([np.asarray(positions, np.int32), np.zeros(pad, np.int32)])
@@ -538,7 +640,7 @@ class DecodeEngine:
             return
         rows = min(chunk, n)
         if self.pre is None or self.pre.rows < rows:
-            self.pre = RowBuffers(rows, self.cfg, self.max_seq, self.device, logits=False)
+            self.pre = RowBuffers(rows, self.cfg, self.max_seq, self.device, logits=False, heads=self.nh_local)
         b = self.pre
         t_d = torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device)
         p_d = torch.as_tensor(np.asarray(positions, np.int32)).to(self.device)
@@ -563,6 +665,11 @@ class DecodeEngine:
         """Kernels of this library one step launches (for reporting)."""
         L0 = self.layers[0]
         small = M <= _lib.lib().orch_gemv_max_rows()  # the GEMV normalises its own rows
+        if self.heads_split:  # norm (above 8 rows) + qkv, attention, o, norm + gate/up, down
+            per_layer = 5 + (0 if small else 2)
+            if _lib.lib().orch_attention_workspace_bytes(M, self.nh_local, self.cfg.head_dim, self.max_seq) > 0:
+                per_layer += 1
+            return 1 + per_layer * len(self.layers) + (4 if logits else 0)
         per_layer = 7 + len(L0.lora)
         per_layer -= int(L0.tiled and "qkv" not in L0.lora and small)
         per_layer -= int(L0.tiled and self.split is None and "gu" not in L0.lora and small)
@@ -622,15 +729,20 @@ class DecodeEngine:
 # --------------------------------------------------------------------------------------
 
 class Llama:
-    """``orchard.Llama`` on B200 (orchard/model.py:197-381)."""
+    """``orchard.Llama`` on B200 (orchard/model.py:197-381).
+
+    ``group`` (a torch.distributed NCCL group, one GPU per rank) splits the model over the
+    ranks: by default each rank passes its own sequences and the FFN and vocabulary
+    projections are split by columns; with ``split_heads`` every rank passes the same
+    sequences and the attention heads are split as well (parallel.py)."""
 
     def __init__(self, model_path: Optional[str] = None, *, checkpoint: Optional[Checkpoint] = None,
                  device=0, max_batch: int = 32, max_seq: Optional[int] = None, tokenizer=None,
-                 use_graphs: bool = True, tiled: bool = True, group=None):
+                 use_graphs: bool = True, tiled: bool = True, group=None, split_heads: bool = False):
         ck = checkpoint if checkpoint is not None else load_checkpoint(model_path)
         self.config = dict(ck.config)
         self.engine = DecodeEngine(ck, device=device, max_batch=max_batch, max_seq=max_seq, tiled=tiled,
-                                   group=group)
+                                   group=group, split_heads=split_heads)
         self.use_graphs = use_graphs
         self.tokenizer = tokenizer
         if tokenizer is None and model_path is not None:

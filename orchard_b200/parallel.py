@@ -1,8 +1,8 @@
-"""Column split of the large-N projections across the GPUs of one box.
+"""Column split of the large-N projections across the GPUs of one box, and the head split.
 
-Sequences are sharded data-parallel (each rank owns ``B / world`` rows with their KV cache,
-attention and Q/K/V/O projections, whose weights every rank holds), and the two large-N
-projections are split by columns:
+Two arrangements. In the column split sequences are sharded data-parallel (each rank owns
+``B / world`` rows with their KV cache, attention and Q/K/V/O projections, whose weights
+every rank holds), and the two large-N projections are split by columns:
 
 * FFN: rank r holds gate/up rows ``F[f0:f1]`` and the matching down-projection columns
   ``W2[:, f0:f1]`` (a K split). Per layer: all-gather the normed hidden state of every
@@ -12,6 +12,15 @@ projections are split by columns:
 * vocab: rank r holds lm_head rows ``V[v0:v1]``; after the final norm the rows are
   all-gathered, each rank takes the (max, argmax) of its vocabulary slice, the pairs are
   all-gathered and merged (highest logit, lowest id on ties, as ``np.argmax``).
+
+The head split (``ColumnSplit.plan(..., num_heads=nh)``) also divides the attention: every
+rank runs all rows (the residual is the same on every rank), rank r holds attention heads
+``[h0, h1)``: those heads' rows of Wq / Wk / Wv, their K/V cache, and the O projection's
+columns ``Wo[:, h0*hd:h1*hd]`` (a K split), beside the FFN and vocabulary slices above.
+Per layer two all-reduces of the fp32 residual: after the O projection and after the down
+projection, each rank adding its partial sum over K and rank 0 also the residual itself.
+Nothing of the model is replicated, so at batch 1 every weight byte and every KV byte is
+read by one rank only.
 
 This module holds the split arithmetic and the order of operations; the device buffers,
 kernels and collectives are supplied by the caller (``ops`` / ``comm`` objects), so the
@@ -56,16 +65,37 @@ class ColumnSplit:
     f1: int
     v0: int
     v1: int
+    h0: int = 0  # attention heads [h0, h1) of the head split; h1 == 0: heads not split
+    h1: int = 0
 
     @classmethod
-    def plan(cls, intermediate_size: int, vocab_size: int, world: int, rank: int) -> "ColumnSplit":
+    def plan(cls, intermediate_size: int, vocab_size: int, world: int, rank: int,
+             num_heads: int = 0, head_dim: int = 0) -> "ColumnSplit":
+        """``num_heads`` > 0 plans the head split as well (``head_dim`` a multiple of 32, so
+        each rank's slice of the O projection's K starts on a scale group)."""
         # FFN slices: multiples of 32 (one INT4 scale group, so the down projection's K
         # slice starts on a group; also the gate/up interleave's 16-row blocks)
         f0, f1 = shard_range(intermediate_size, world, rank, 32)
         v0, v1 = shard_range(vocab_size, world, rank, 16)
         if f1 <= f0 or v1 <= v0:
             raise ValueError("too many ranks for these projection sizes")
-        return cls(world, rank, f0, f1, v0, v1)
+        h0 = h1 = 0
+        if num_heads:
+            if head_dim <= 0 or head_dim % 32:
+                raise ValueError("the head split needs a head_dim that is a multiple of 32")
+            if num_heads < world:
+                raise ValueError(f"{world} ranks cannot split {num_heads} attention heads")
+            h0, h1 = shard_range(num_heads, world, rank, 1)
+        return cls(world, rank, f0, f1, v0, v1, h0, h1)
+
+    @property
+    def heads(self) -> bool:
+        """True for the head split (rows replicated, attention heads divided)."""
+        return self.h1 > 0
+
+    @property
+    def h_local(self) -> int:
+        return self.h1 - self.h0
 
     @property
     def f_local(self) -> int:
@@ -86,6 +116,16 @@ class ColumnSplit:
     def lm_shard(self, w, s):
         """lm_head rows ``v0:v1`` (packed and scales)."""
         return w[self.v0:self.v1], s[self.v0:self.v1]
+
+    def attn_shard(self, wq, sq, wk, sk, wv, sv, wo, so, head_dim: int):
+        """Slices of packed INT4 attention weights for heads ``h0:h1``: the rows
+        ``h0*hd:h1*hd`` of Wq, Wk and Wv, and the same range of the O projection's columns
+        (bytes ``/2``, scale groups ``/32``)."""
+        if not self.heads:
+            raise ValueError("this plan does not split the heads")
+        r0, r1 = self.h0 * head_dim, self.h1 * head_dim
+        return (wq[r0:r1], sq[r0:r1], wk[r0:r1], sk[r0:r1], wv[r0:r1], sv[r0:r1],
+                wo[:, r0 // 2:r1 // 2], so[:, r0 // 32:r1 // 32])
 
 
 def merge_argmax(vals: np.ndarray, idx: np.ndarray) -> np.ndarray:
@@ -138,3 +178,44 @@ def head_column_split(ops, comm, bufs, rows: int) -> None:
     ops.argmax_pairs(bufs.logits, bufs.pairs, rows * comm.world)
     comm.all_gather(bufs.pairs_all, bufs.pairs, rows * comm.world)
     ops.merge_pairs(bufs.pairs_all, bufs.tok, rows)
+
+
+# ------------------------------------------------------------------------------------------
+# head split: every rank runs all rows; attention heads, FFN and vocabulary divided
+# ------------------------------------------------------------------------------------------
+
+def attention_head_split(ops, comm, layer, bufs, rows: int) -> None:
+    """Attention half of one layer for all ``rows`` rows (the residual ``bufs.x`` is the same
+    on every rank):
+
+        q, k, v = rmsnorm(x) [Wq; Wk; Wv][heads h0:h1]^T, RoPE, k / v into this rank's cache
+        a       = attention(q, k, v)                 this rank's heads
+        x       = x + a Wo[:, h0:h1]^T  on rank 0,   a Wo[:, h0:h1]^T  on the others (fp32)
+        x       = all_reduce_sum(x)
+    """
+    ops.qkv_local(layer, bufs, rows)
+    ops.attention_local(layer, bufs, rows)
+    ops.o_partial(layer, bufs, rows, comm.rank == 0)
+    comm.all_reduce(bufs.x, rows)
+
+
+def ffn_head_split(ops, comm, layer, bufs, rows: int) -> None:
+    """FFN half of one layer for all ``rows`` rows:
+
+        h = silu(rmsnorm(x) Wg[f0:f1]^T) * (rmsnorm(x) Wu[f0:f1]^T)
+        x = x + h W2[:, f0:f1]^T  on rank 0,  h W2[:, f0:f1]^T  on the others (fp32)
+        x = all_reduce_sum(x)
+    """
+    ops.gate_up_local(layer, bufs, rows)
+    ops.down_partial_resid(layer, bufs, rows, comm.rank == 0)
+    comm.all_reduce(bufs.x, rows)
+
+
+def vocab_head_split(ops, comm, bufs, rows: int) -> None:
+    """Final norm and the vocabulary-split lm_head for all ``rows`` rows: each rank's
+    (max, id) pair per row, gathered and merged; ``bufs.tok`` receives every row's token."""
+    ops.rmsnorm(bufs.x, None, bufs.xn, rows)
+    ops.lm_partial(bufs.xn, bufs.logits, rows)
+    ops.argmax_pairs(bufs.logits, bufs.pairs, rows)
+    comm.all_gather(bufs.pairs_all, bufs.pairs, rows)
+    ops.merge_all_pairs(bufs.pairs_all, bufs.tok, rows)

@@ -1,9 +1,11 @@
-"""The column split on two GPUs (skipped with fewer): two ranks (NCCL) each own one of the
-tiny checkpoint's two sequences and half of its FFN and vocabulary columns; greedy
-``generate_batch_ids`` on each rank must reproduce the tokens the reference's own
-``orchard/model.py`` produced for that sequence (tests/golden/tiny_model.npz), with the
-decode step captured in CUDA graphs and eagerly. The prompts have different lengths, so
-the shorter rank's prefill is padded into the scratch slot."""
+"""The column split and the head split on two GPUs (skipped with fewer).
+
+Column split: two ranks (NCCL) each own one of the tiny checkpoint's two sequences and half
+of its FFN and vocabulary columns; greedy ``generate_batch_ids`` on each rank must
+reproduce the tokens the reference's own ``orchard/model.py`` produced for that sequence
+(tests/golden/tiny_model.npz), with the decode step captured in CUDA graphs and eagerly.
+The prompts have different lengths, so the shorter rank's prefill is padded into the
+scratch slot. Head split: both ranks run both sequences, each with half of the heads."""
 
 import os
 import socket
@@ -23,7 +25,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, graphs, q):
+def _rank(rank, world, port, graphs, q, heads=False):
     import datetime
     import json
 
@@ -42,9 +44,14 @@ def _rank(rank, world, port, graphs, q):
         cfg = json.loads(str(z["config_json"]))
         ckpt = {k[len("ckpt/"):]: z[k] for k in z.files if k.startswith("ckpt/")}
         prompts = [[int(v) for v in p if v >= 0] for p in z["prompts"]]
-        llm = Llama.from_tensors(cfg, ckpt, device=rank, max_batch=2, use_graphs=graphs, group=dist.group.WORLD)
-        toks = llm.generate_batch_ids([prompts[rank]], max_tokens=int(z["max_tokens"]), temperature=0)
-        q.put((rank, toks[0], None))
+        llm = Llama.from_tensors(cfg, ckpt, device=rank, max_batch=2, use_graphs=graphs, group=dist.group.WORLD,
+                                 split_heads=heads)
+        if heads:  # every rank runs both sequences with one of the two heads
+            toks = llm.generate_batch_ids(prompts, max_tokens=int(z["max_tokens"]), temperature=0)
+            q.put((rank, toks, None))
+        else:
+            toks = llm.generate_batch_ids([prompts[rank]], max_tokens=int(z["max_tokens"]), temperature=0)
+            q.put((rank, toks[0], None))
     except Exception as e:  # reported to the parent
         q.put((rank, None, repr(e)))
     finally:
@@ -74,3 +81,29 @@ def test_column_split_two_gpus_matches_reference_golden(graphs):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert [got[0], got[1]] == ref
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("graphs", [True, False])
+def test_head_split_two_gpus_matches_reference_golden(graphs):
+    """The head split: both ranks run both sequences, each holding one of the tiny model's two
+    attention heads (its Q/K/V rows, O columns and KV cache) and half of the FFN and
+    vocabulary; both must produce the reference's golden tokens for both sequences."""
+    import torch.multiprocessing as mp
+    z = np.load(GOLDEN)
+    ref = [[int(v) for v in t if v >= 0] for t in z["tokens"]]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, graphs, q, True)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, t, err = q.get(timeout=300)
+        assert err is None, err
+        got[r] = t
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert got[0] == ref and got[1] == ref

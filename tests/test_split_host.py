@@ -5,6 +5,12 @@ The split plan (which FFN / vocabulary columns a rank holds), the merge of per-r
 ``head_column_split`` are checked here with NumPy kernels built on the oracle: two ranks
 each hold half of the FFN columns and half of the vocabulary, and their result must equal
 the unsplit computation (fp32 sums split in K: max-rel <= 1e-5; tokens exact).
+
+The head split (``attention_head_split`` / ``ffn_head_split`` / ``vocab_head_split``) is
+checked the same way against the oracle's own layer (``OracleModel.layer_forward``, which
+restates orchard/model.py:78-195): two ranks with half of the attention heads (their Q/K/V
+rows, O columns and KV cache) each, all rows on both ranks, bit-identical residuals after
+the all-reduces.
 """
 
 import os
@@ -214,3 +220,164 @@ def test_column_split_two_gloo_ranks_match_unsplit():
     tok_split = np.concatenate([res[r][1] for r in range(world)])
     assert np.abs(x_split - x_ref).max() / np.abs(x_ref).max() <= 1e-5
     assert np.array_equal(tok_split, tok_ref)
+
+
+# ------------------------------------------------------------------------------------------
+# the head split: two gloo ranks, each with half the attention heads, FFN and vocabulary,
+# run one decode step of every row; the result must equal the oracle's unsplit layer
+# ------------------------------------------------------------------------------------------
+
+HCFG = {"hidden_size": 128, "num_attention_heads": 4, "intermediate_size": 192, "num_hidden_layers": 1,
+        "vocab_size": 64, "rms_norm_eps": 1e-5, "max_position_embeddings": 64}
+HPOS = [5, 3, 7]  # each row's position; its cache holds positions 0 .. pos-1
+
+
+def head_split_case():
+    """The oracle model, the rows' input residual and their caches (N(0,1), all heads)."""
+    from oracle.model import random_model
+    m, _ = random_model(HCFG, seed=5)
+    H, nh = HCFG["hidden_size"], HCFG["num_attention_heads"]
+    hd = H // nh
+    g = np.random.default_rng(17)
+    x = g.standard_normal((len(HPOS), H)).astype(np.float32)
+    kc = [g.standard_normal((nh, p, hd)).astype(np.float32) for p in HPOS]
+    vc = [g.standard_normal((nh, p, hd)).astype(np.float32) for p in HPOS]
+    return m, x, kc, vc
+
+
+class NpHeadOps:
+    """The head split's ops interface (parallel.py) with oracle arithmetic on this rank's
+    slices; bufs hold CPU torch tensors, the cache is a list of per-row arrays."""
+
+    def __init__(self, m, plan, kc, vc):
+        L = m.layers[0]
+        self.m, self.p, self.hd = m, plan, HCFG["hidden_size"] // HCFG["num_attention_heads"]
+        wq, sq, wk, sk, wv, sv, wo, so = plan.attn_shard(*L.wq, *L.wk, *L.wv, *L.wo, self.hd)
+        w1, s1, w3, s3, w2, s2 = plan.ffn_shard(*L.w1, *L.w3, *L.w2)
+        c = np.ascontiguousarray
+        self.wq, self.wk, self.wv = (wq, sq), (wk, sk), (wv, sv)
+        self.wo, self.w1, self.w3, self.w2 = (c(wo), c(so)), (w1, s1), (w3, s3), (c(w2), c(s2))
+        self.lm = plan.lm_shard(*m.lm_head)
+        self.kc = [k[plan.h0:plan.h1] for k in kc]
+        self.vc = [v[plan.h0:plan.h1] for v in vc]
+        self.L = L
+
+    def qkv_local(self, ctx, b, rows):
+        x = b.x[:rows].numpy()
+        xn = ops.rmsnorm(x, self.L.attn_norm, EPS)
+        hl = self.p.h_local
+        cos, sin = self.m.freqs_cos[HPOS], self.m.freqs_sin[HPOS]
+        q = ops.rope(ops.gemm_q4_0(*self.wq, xn).reshape(rows, hl, self.hd), cos, sin)
+        k = ops.rope(ops.gemm_q4_0(*self.wk, xn).reshape(rows, hl, self.hd), cos, sin)
+        v = ops.gemm_q4_0(*self.wv, xn).reshape(rows, hl, self.hd)
+        for i in range(rows):
+            self.kc[i] = np.concatenate([self.kc[i], k[i][:, None, :]], axis=1)
+            self.vc[i] = np.concatenate([self.vc[i], v[i][:, None, :]], axis=1)
+        b.q = q
+
+    def attention_local(self, ctx, b, rows):
+        b.attn = np.stack([ops.attention_one(b.q[i], self.kc[i], self.vc[i]).reshape(-1) for i in range(rows)])
+
+    def o_partial(self, ctx, b, rows, resid):
+        p = torch.from_numpy(ops.gemm_q4_0(*self.wo, b.attn).astype(np.float32))
+        b.x[:rows] = b.x[:rows] + p if resid else p
+
+    def gate_up_local(self, ctx, b, rows):
+        xf = ops.rmsnorm(b.x[:rows].numpy(), self.L.ffn_norm, EPS)
+        b.h = ops.mul(ops.silu(ops.gemm_q4_0(*self.w1, xf)), ops.gemm_q4_0(*self.w3, xf))
+
+    def down_partial_resid(self, ctx, b, rows, resid):
+        p = torch.from_numpy(ops.gemm_q4_0(*self.w2, b.h).astype(np.float32))
+        b.x[:rows] = b.x[:rows] + p if resid else p
+
+    def rmsnorm(self, x, w, xn, rows):
+        xn[:rows] = torch.from_numpy(ops.rmsnorm(x[:rows].numpy(), self.m.norm, EPS))
+
+    def lm_partial(self, xn, logits, rows):
+        logits[:rows] = torch.from_numpy(ops.gemm_q4_0(*self.lm, xn[:rows].numpy()).astype(np.float32))
+
+    def argmax_pairs(self, logits, pairs, rows):
+        lg = logits[:rows].numpy()
+        i = np.argmax(lg, axis=1)
+        pairs[:rows, 0] = torch.from_numpy(lg[np.arange(rows), i])
+        pairs[:rows, 1] = torch.from_numpy((self.p.v0 + i).astype(np.float32))
+
+    def merge_all_pairs(self, pairs_all, tok, rows):
+        pa = pairs_all[:self.p.world * rows].numpy().reshape(self.p.world, rows, 2)
+        tok[:rows] = torch.from_numpy(merge_argmax(pa[..., 0], pa[..., 1].astype(np.int64)).astype(np.int32))
+
+
+class HeadComm(GlooComm):
+    def all_reduce(self, x, rows):
+        dist.all_reduce(x[:rows])
+
+
+class HeadBufs:
+    def __init__(self, plan, x):
+        R, H = x.shape
+        self.x = torch.from_numpy(x.copy())
+        self.xn = torch.zeros((R, H), dtype=torch.float32)
+        self.logits = torch.zeros((R, plan.v_local), dtype=torch.float32)
+        self.pairs = torch.zeros((R, 2), dtype=torch.float32)
+        self.pairs_all = torch.zeros((plan.world * R, 2), dtype=torch.float32)
+        self.tok = torch.zeros(R, dtype=torch.int32)
+
+
+def _head_rank(rank, world, port, q):
+    from orchard_b200.parallel import attention_head_split, ffn_head_split, vocab_head_split
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, x, kc, vc = head_split_case()
+        hd = HCFG["hidden_size"] // HCFG["num_attention_heads"]
+        plan = ColumnSplit.plan(HCFG["intermediate_size"], HCFG["vocab_size"], world, rank,
+                                HCFG["num_attention_heads"], hd)
+        o, c, b = NpHeadOps(m, plan, kc, vc), HeadComm(world, rank), HeadBufs(plan, x)
+        attention_head_split(o, c, None, b, len(HPOS))
+        ffn_head_split(o, c, None, b, len(HPOS))
+        x_after = b.x.numpy().copy()
+        vocab_head_split(o, c, b, len(HPOS))
+        q.put((rank, x_after, b.tok.numpy().copy(), plan.h0, plan.h1))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_split_plan():
+    parts = [ColumnSplit.plan(11008, 32000, 8, r, 32, 128) for r in range(8)]
+    assert [(p.h0, p.h1) for p in parts] == [(4 * r, 4 * r + 4) for r in range(8)]
+    assert all(p.heads for p in parts) and not ColumnSplit.plan(11008, 32000, 8, 0).heads
+    with pytest.raises(ValueError):
+        ColumnSplit.plan(11008, 32000, 8, 0, 4, 128)  # fewer heads than ranks
+    with pytest.raises(ValueError):
+        ColumnSplit.plan(11008, 32000, 2, 0, 32, 48)  # O columns would split a scale group
+    with pytest.raises(ValueError):
+        ColumnSplit.plan(11008, 32000, 2, 0).attn_shard(*([None] * 8), 128)
+
+
+def test_head_split_two_gloo_ranks_match_oracle_layer():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_head_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, x, t, h0, h1 = q.get(timeout=120)
+        res[r] = (x, t, h0, h1)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [(res[r][2], res[r][3]) for r in range(world)] == [(0, 2), (2, 4)]
+    # unsplit: the oracle's own layer (orchard/model.py:78-195) over the same caches
+    m, x, kc, vc = head_split_case()
+    for i, (k, v) in enumerate(zip(kc, vc)):
+        m.k_cache[0][i], m.v_cache[0][i] = k, v
+    x_ref = m.layer_forward(0, x, m.freqs_cos[HPOS], m.freqs_sin[HPOS], list(range(len(HPOS))))
+    tok_ref = np.argmax(m._lin(m.lm_head, ops.rmsnorm(x_ref, m.norm, EPS)), axis=1)
+    for r in range(world):  # every rank holds every row, bit-identical after the all-reduces
+        assert np.array_equal(res[r][0], res[0][0])
+        assert np.array_equal(res[r][1], tok_ref)
+    assert np.abs(res[0][0] - x_ref).max() / np.abs(x_ref).max() <= 1e-5
