@@ -178,13 +178,21 @@ SPLIT_FAMILIES = {"orch_q4t_qkv_rope": "attn_proj_gemm (replicated weights)",
                   "orch_q4t_linear_resid": "attn_proj_gemm (replicated weights)",
                   "orch_q4t_linear_swiglu": "ffn_vocab_slice_gemm", "orch_q4t_gemm": "ffn_vocab_slice_gemm",
                   "nccl": "nccl", "orch_attention_decode": "attention"}
+# the head split: every projection is a slice; the all-reduces are timed around the
+# collective (peer-memory kernel or NCCL), so the peer kernel's own launch is not counted twice
+HEAD_FAMILIES = {"orch_q4t_rms_qkv_rope": "slice_gemm", "orch_q4t_qkv_rope": "slice_gemm",
+                 "orch_q4t_linear_resid": "slice_gemm", "orch_q4t_rms_linear_swiglu": "slice_gemm",
+                 "orch_q4t_linear_swiglu": "slice_gemm", "orch_q4t_gemm": "slice_gemm",
+                 "nccl": "allreduce / all-gather", "orch_peer_allreduce": None,
+                 "orch_attention_decode": "attention"}
 
 
 def kernel_profile(llm, B, pos, reps=3, split=False):
     """Per-kernel-family device time of one eager decode step (CUDA events around each
     launch on the launching stream), with each family's algorithmic bytes. With `split`
     (the column split) the families are the replicated attention projections, the FFN /
-    vocabulary slice GEMMs, attention, the NCCL collectives and the rest."""
+    vocabulary slice GEMMs, attention, the NCCL collectives and the rest; for the head split,
+    the slice GEMMs, attention, the all-reduces / all-gather and the rest."""
     import torch
 
     from orchard_b200 import _lib
@@ -218,7 +226,7 @@ def kernel_profile(llm, B, pos, reps=3, split=False):
         return rc
 
     if split and comm is not None:
-        for nm in ("all_gather", "reduce_scatter"):
+        for nm in ("all_gather", "reduce_scatter", "all_reduce"):
             saved[nm] = getattr(comm, nm)
             setattr(comm, nm, lambda *args, _fn=saved[nm]: timed_collective(_fn, *args))
 
@@ -234,8 +242,11 @@ def kernel_profile(llm, B, pos, reps=3, split=False):
     L = pos + 1
     out = {}
     if split:
+        table = HEAD_FAMILIES if getattr(eng, "heads_split", False) else SPLIT_FAMILIES
         for name, ev in fam.items():
-            key = SPLIT_FAMILIES.get(name, "other")
+            key = table.get(name, "other")
+            if key is None:
+                continue
             d = out.setdefault(key, {"ms": 0.0, "launches": 0})
             d["ms"] += sum(a.elapsed_time(b) for a, b, _ in ev) / reps
             d["launches"] += len(ev) // reps
@@ -447,6 +458,8 @@ def time_head_split(cfg, dev, batches, steps, warmup, world, check_steps=8):
         secs = float(t.item())
         out["by_global_batch"][str(B)] = {"tok_s": round(B * steps / secs, 2),
                                           "ms_per_step": round(secs / steps * 1000, 4), "steps": steps}
+        fam = kernel_profile(llm, B, start + warmup + steps // 2, split=True)
+        out["by_global_batch"][str(B)]["families_ms"] = {k: round(v["ms"], 4) for k, v in fam.items()}
     v0, v1 = sp.v0, sp.v1
     eng.release_graphs()
     del llm, eng

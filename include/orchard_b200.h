@@ -58,8 +58,8 @@ int orch_device_name(char* buf, size_t len);
  * table (that row's q/k/v not written); 2 an attention row's position outside the cache
  * or a bad prefill unit (its output not written); 4 an embedding id outside the vocabulary
  * (zero row); 8 a cache slot outside [0, num_slots) (no cache read or write for that row);
- * 256 a tensor-core GEMM's bounded wait ran out. Covers the allocation-free attention
- * entry point's flags as well. */
+ * 256 a tensor-core GEMM's bounded wait ran out; 512 a peer all-reduce's wait for another
+ * rank ran out. Covers the allocation-free attention entry point's flags as well. */
 int orch_device_check(uint32_t* flags_out, void* stream);
 
 /* ---- buffers (metal_backend.h:19-22; tensor.cpp:17-72) -------------------------------- */
@@ -291,6 +291,26 @@ int orch_argmax_rows(const float* logits, uint32_t M, uint32_t V, int32_t* out, 
 /* Gathers fp32 residual rows x[m] = table[ids[m]] (table fp16 or fp32 [V, H]). */
 int orch_embed_rows(const int32_t* ids, const void* table, int table_dt, float* x, uint32_t M,
                     uint32_t H, uint32_t V, void* stream);
+
+/* ---- peer-memory all-reduce of the head split ------------------------------------------
+ * The reference runs on one device (orchard/model.py:78-195 has no collective); the head
+ * split's order of operations (orchard_b200/parallel.py: attention_head_split,
+ * ffn_head_split) sums the fp32 residual over the ranks after the O and the down
+ * projections. One process per GPU of one box. Each rank allocates a region of
+ * orch_peer_region_bytes(world, max_floats) bytes (orch_alloc), zeroes it, exports it with
+ * orch_ipc_handle (64 bytes), and opens every other rank's handle with orch_ipc_open; after
+ * a barrier (so no rank writes into a region before it is zeroed) orch_peer_allreduce sums
+ * x[0..n) over the ranks in place: bases[q] is rank q's region as mapped here (own included),
+ * the same world and max_floats the regions were sized with; n <= max_floats, both multiples
+ * of 4; every rank makes the same calls in the same order. The result is the same bits on
+ * every rank (slots added in rank order). A wait for a peer that runs out (~5 s) sets device
+ * check bit 512. Regions and mappings live until orch_ipc_close / orch_free. */
+size_t orch_peer_region_bytes(uint32_t world, uint32_t max_floats);
+int orch_ipc_handle(void* base, void* handle_out);
+int orch_ipc_open(const void* handle, void** base_out);
+int orch_ipc_close(void* base);
+int orch_peer_allreduce(void* const* bases, uint32_t rank, uint32_t world, uint32_t max_floats,
+                        float* x, uint32_t n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -99,6 +99,11 @@ _SIGS = {
     "orch_attention_decode_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp]),
     "orch_argmax_rows": (_i32, [_vp, _u32, _u32, _vp, _vp]),
     "orch_embed_rows": (_i32, [_vp, _vp, _i32, _vp, _u32, _u32, _u32, _vp]),
+    "orch_peer_region_bytes": (_sz, [_u32, _u32]),
+    "orch_ipc_handle": (_i32, [_vp, _vp]),
+    "orch_ipc_open": (_i32, [_vp, C.POINTER(_vp)]),
+    "orch_ipc_close": (_i32, [_vp]),
+    "orch_peer_allreduce": (_i32, [_vp, _u32, _u32, _u32, _vp, _u32, _vp]),
 }
 
 _lock = threading.Lock()

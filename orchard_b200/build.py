@@ -26,7 +26,7 @@ LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "liborchard_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["capi.cu", "qgemm.cu", "tcgemm.cu", "tcgemm_sk.cu", "gemv.cu", "attention.cu", "attention_prefill.cu", "elementwise.cu", "quantize.cu"]
+CU_SOURCES = ["capi.cu", "qgemm.cu", "tcgemm.cu", "tcgemm_sk.cu", "gemv.cu", "attention.cu", "attention_prefill.cu", "elementwise.cu", "quantize.cu", "peer_allreduce.cu"]
 CORE_SOURCES = ["core_backend.cpp", "core_bindings.cpp"]
 
 

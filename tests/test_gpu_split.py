@@ -107,3 +107,65 @@ def test_head_split_two_gpus_matches_reference_golden(graphs):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert got[0] == ref and got[1] == ref
+
+
+def _ar_rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from orchard_b200._lib import call
+        from orchard_b200.model import _PeerAllReduce
+        call("orch_init", rank, None)
+        H, rows_max = 4096, 8
+        ar = _PeerAllReduce(dist.group.WORLD, world, rank, rows_max * H, dev)
+        ok = []
+        for it, rows in enumerate([1, 8, 3, 8, 1, 2, 5]):  # block counts 1..8, both banks
+            g = torch.Generator(device=dev).manual_seed(1000 * it + rank)
+            x = torch.randn((rows_max, H), generator=g, device=dev)
+            parts = [torch.empty((rows, H), device=dev) for _ in range(world)]
+            dist.all_gather(parts, x[:rows].contiguous())
+            want = parts[0].clone()
+            for p in parts[1:]:
+                want += p  # rank order, fp32: the kernel's order
+            tail = x[rows:].clone()
+            ar(x, rows * H)
+            torch.cuda.synchronize(dev)
+            ok.append(bool(torch.equal(x[:rows], want)) and bool(torch.equal(x[rows:], tail)))
+        import ctypes as C
+        flags = C.c_uint32(0)
+        call("orch_device_check", C.byref(flags), torch.cuda.current_stream(dev).cuda_stream)
+        q.put((rank, ok, flags.value, None))
+    except Exception as e:
+        q.put((rank, None, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_allreduce_two_gpus_bit_exact():
+    """orch_peer_allreduce over two GPUs equals the rank-ordered fp32 sum of the gathered
+    inputs, bit for bit, on every rank, over calls of 1..8 rows (both banks of slots)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ar_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for _ in range(2):
+        r, ok, flags, err = q.get(timeout=300)
+        assert err is None, err
+        assert all(ok), ok
+        assert flags == 0
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
