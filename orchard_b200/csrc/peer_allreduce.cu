@@ -4,22 +4,23 @@
 // The reference runs on one device and has no collective; the split's order of operations
 // (orchard_b200/parallel.py) names an all-reduce after the O and the down projections. At
 // decode sizes (16 KB per row) a library all-reduce is latency-bound, so this one takes a
-// single launch and one NVLink crossing:
+// single launch and one NVLink crossing, with no fence and no separate flag:
 //
-//  * every rank owns a region (cudaMalloc'd here, mapped by the other ranks through CUDA
-//    IPC): a header (call counter, block counter), flags [8 ranks][64 blocks] and two
-//    banks of receive slots [2][world][cap] fp32, used on alternate calls;
-//  * block b of rank r stores its chunk of x into slot r of bank (call & 1) on every rank
-//    (plain stores over NVLink; no multicast), then, after a system-scope fence, writes
-//    the call number into flag [r][b] on every rank with a release store;
-//  * it waits (acquire loads, bounded by ~5 s of globaltimer) until flag [q][b] of its own
-//    region holds this call's number for every rank q, and writes x = sum over q of slot q,
-//    added in rank order: every rank computes the same bits.
+//  * every rank owns a region (cudaMalloc'd by the caller, mapped by the other ranks through
+//    CUDA IPC): a header (call counter, block counter) and two banks of receive slots
+//    [2][world][cap] of 64-bit words, used on alternate calls;
+//  * each word carries one fp32 value in its low half and the call number in its high half,
+//    so one aligned 8-byte store delivers both at once (single-copy atomic);
+//  * thread j of rank r stores its two values of x into slot r of bank (call & 1) on every
+//    rank (16-byte relaxed system-scope stores over NVLink; no multicast), then polls the
+//    same two words of every slot q in its own region (relaxed system-scope loads, all ranks'
+//    loads in flight together, bounded by ~5 s of globaltimer) until they carry this call's
+//    number, and writes x = sum over q, added in rank order: every rank computes the same bits.
 //
-// Two banks suffice: a rank can only start call k + 2 after every rank's flags of call
-// k + 1, which each rank writes after its call k (the one reading bank k & 1) has ended.
-// On a wait that runs out the block sets device check bit 512, sums what it has and the
-// call counters still advance.
+// Two banks suffice: a rank can only start call k + 2 after it has read every rank's words
+// of call k + 1, which each rank writes after its call k (the one reading bank k & 1) has
+// ended. On a wait that runs out the thread sets device check bit 512 and sums what it has;
+// the call counters still advance.
 #include <algorithm>
 #include <cstring>
 
@@ -30,31 +31,30 @@ namespace orch {
 constexpr int kArMaxRanks = 8;
 constexpr int kArMaxBlocks = 64;
 constexpr int kArThreads = 256;
-constexpr size_t kArFlagsOff = 256;   // after the header: epoch, block counter
-constexpr size_t kArSlotsOff = 4096;  // flags take 8 x 64 x 4 = 2 KB
+constexpr size_t kArSlotsOff = 4096;  // after the header: call counter, block counter
 
 struct ArArgs {
   char* base[kArMaxRanks];  // every rank's region as mapped on this device (own included)
   float* x;
   uint32_t* check;
   int rank, world;
-  int n4;       // float4s to reduce
-  int per_blk;  // float4s per block
-  size_t cap4;  // float4s per receive slot
+  int npairs;   // pairs of floats to reduce
+  size_t cap2;  // pairs per receive slot
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_v2(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_relaxed_sys_v2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
+}
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t e) {
+  return ((uint64_t)e << 32) | (uint64_t)__float_as_uint(v);
 }
 
 __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(ArArgs a) {
@@ -63,53 +63,56 @@ __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(ArArgs a) {
   uint32_t* hdr = reinterpret_cast<uint32_t*>(own);
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(hdr) + 1u;  // this call's number
   const size_t bank = e & 1u;
-  const int b = blockIdx.x;
-  const int i0 = b * a.per_blk;
-  const int i1 = min(a.n4, i0 + a.per_blk);
-  const float4* x4 = reinterpret_cast<const float4*>(a.x);
+  const int stride = gridDim.x * kArThreads;
+  const float2* x2 = reinterpret_cast<const float2*>(a.x);
+  float2* xo = reinterpret_cast<float2*>(a.x);
 
-  // 1. this rank's chunk into slot `rank` of the bank, on every rank
-  const size_t my_slot = (bank * a.world + a.rank) * a.cap4;
-  for (int i = i0 + threadIdx.x; i < i1; i += kArThreads) {
-    const float4 v = x4[i];
-    for (int q = 0; q < a.world; ++q)
-      reinterpret_cast<float4*>(a.base[q] + kArSlotsOff)[my_slot + i] = v;
+  // 1. this rank's values into slot `rank` of the bank, on every rank
+  const size_t my_slot = (bank * a.world + a.rank) * a.cap2;
+  for (int j = blockIdx.x * kArThreads + threadIdx.x; j < a.npairs; j += stride) {
+    const float2 v = x2[j];
+    const uint64_t w0 = ll_word(v.x, e), w1 = ll_word(v.y, e);
+#pragma unroll
+    for (int q = 0; q < kArMaxRanks; ++q)
+      if (q < a.world)
+        st_relaxed_sys_v2(reinterpret_cast<uint64_t*>(a.base[q] + kArSlotsOff) + 2 * (my_slot + j), w0, w1);
   }
-  __syncthreads();
-  // 2. publish: flag [rank][b] = e on every rank, after a system-scope fence
-  if (threadIdx.x < a.world) {
-    __threadfence_system();
-    uint32_t* f = reinterpret_cast<uint32_t*>(a.base[threadIdx.x] + kArFlagsOff) + a.rank * kArMaxBlocks + b;
-    st_release_sys(f, e);
-  }
-  // 3. wait for every rank's chunk b in this rank's region (bounded)
-  if (threadIdx.x < a.world) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(own + kArFlagsOff) + threadIdx.x * kArMaxBlocks + b;
-    const uint64_t t0 = global_ns();
-    while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
-      if (global_ns() - t0 > 5000000000ull) {
-        atomicOr(a.check, 512u);
-        break;
+  // 2. every rank's values of the same pairs from this rank's region, summed in rank order
+  const uint64_t* slots = reinterpret_cast<const uint64_t*>(own + kArSlotsOff) + 2 * bank * a.world * a.cap2;
+  for (int j = blockIdx.x * kArThreads + threadIdx.x; j < a.npairs; j += stride) {
+    uint64_t w[kArMaxRanks][2];
+    uint32_t pending = 0;
+#pragma unroll
+    for (int q = 0; q < kArMaxRanks; ++q)
+      if (q < a.world) {
+        ld_relaxed_sys_v2(slots + 2 * ((size_t)q * a.cap2 + j), w[q][0], w[q][1]);
+        if ((uint32_t)(w[q][0] >> 32) != e || (uint32_t)(w[q][1] >> 32) != e) pending |= 1u << q;
       }
-      __nanosleep(32);
+    if (pending) {
+      const uint64_t t0 = global_ns();
+      while (pending) {
+#pragma unroll
+        for (int q = 0; q < kArMaxRanks; ++q)
+          if (pending & (1u << q)) {
+            ld_relaxed_sys_v2(slots + 2 * ((size_t)q * a.cap2 + j), w[q][0], w[q][1]);
+            if ((uint32_t)(w[q][0] >> 32) == e && (uint32_t)(w[q][1] >> 32) == e) pending &= ~(1u << q);
+          }
+        if (pending && global_ns() - t0 > 5000000000ull) {
+          atomicOr(a.check, 512u);
+          break;
+        }
+      }
     }
+    float2 s = make_float2(__uint_as_float((uint32_t)w[0][0]), __uint_as_float((uint32_t)w[0][1]));
+#pragma unroll
+    for (int q = 1; q < kArMaxRanks; ++q)
+      if (q < a.world) {
+        s.x += __uint_as_float((uint32_t)w[q][0]);
+        s.y += __uint_as_float((uint32_t)w[q][1]);
+      }
+    xo[j] = s;
   }
-  __syncthreads();
-  // 4. x = sum of the slots in rank order (L2 loads: peers wrote them over NVLink)
-  const float4* slots = reinterpret_cast<const float4*>(own + kArSlotsOff) + bank * a.world * a.cap4;
-  float4* xo = reinterpret_cast<float4*>(a.x);
-  for (int i = i0 + threadIdx.x; i < i1; i += kArThreads) {
-    float4 s = __ldcg(slots + i);
-    for (int q = 1; q < a.world; ++q) {
-      const float4 v = __ldcg(slots + (size_t)q * a.cap4 + i);
-      s.x += v.x;
-      s.y += v.y;
-      s.z += v.z;
-      s.w += v.w;
-    }
-    xo[i] = s;
-  }
-  // 5. the last block advances this rank's call counter (every block has read it)
+  // 3. the last block advances this rank's call counter (every block has read it)
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -128,7 +131,7 @@ using namespace orch;
 extern "C" size_t orch_peer_region_bytes(uint32_t world, uint32_t max_floats) {
   if (world == 0 || world > (uint32_t)kArMaxRanks) return 0;
   const size_t cap = ((size_t)max_floats + 3) / 4 * 4;
-  return kArSlotsOff + 2 * (size_t)world * cap * sizeof(float);
+  return kArSlotsOff + 2 * (size_t)world * cap * sizeof(uint64_t);  // a word per value
 }
 
 extern "C" int orch_ipc_handle(void* base, void* handle_out) {
@@ -171,11 +174,10 @@ extern "C" int orch_peer_allreduce(void* const* bases, uint32_t rank, uint32_t w
   a.x = x;
   a.rank = (int)rank;
   a.world = (int)world;
-  a.n4 = (int)(n / 4);
-  a.cap4 = max_floats / 4;
-  // a block per 1024 float4s (4 per thread), at most 64
-  const int nb = std::min(kArMaxBlocks, std::max(1, (a.n4 + 1023) / 1024));
-  a.per_blk = (a.n4 + nb - 1) / nb;
+  a.npairs = (int)(n / 2);
+  a.cap2 = max_floats / 2;
+  // a thread per pair of values, at most 64 blocks (larger buffers loop)
+  const int nb = std::min(kArMaxBlocks, std::max(1, (a.npairs + kArThreads - 1) / kArThreads));
   ORCH_CUDA(launch_k(peer_allreduce_kernel, dim3(nb), dim3(kArThreads), 0, as_stream(stream), dim3(0, 0, 0), a));
   return check_launch("peer_allreduce");
 }

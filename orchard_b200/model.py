@@ -420,6 +420,26 @@ class _PeerAllReduce:
         self.bases_addr = C.addressof(self._bases)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
+        # a known sum over every rank, twice (both banks of slots); the ranks agree on the
+        # outcome, and on a failure they all keep the library collective
+        ok = torch.tensor([1 if self._self_test(device) else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        self.ok = bool(ok.item())
+
+    def _self_test(self, device) -> bool:
+        import ctypes as C
+        n = self.max_floats - self.max_floats % 4
+        pattern = (1 + torch.arange(n, device=device) % 7).float()
+        want = pattern * (self.world * (self.world + 1) // 2)
+        good = True
+        for _ in range(2):
+            x = pattern * (self.rank + 1)
+            self(x, n)
+            torch.cuda.synchronize(device)
+            good = good and bool(torch.equal(x, want))
+        flags = C.c_uint32(0)
+        call("orch_device_check", C.byref(flags), _stream())
+        return good and (flags.value & 512) == 0
 
     def __call__(self, x, n: int):
         call("orch_peer_allreduce", self.bases_addr, self.rank, self.world, self.max_floats, ptr(x), n, _stream())
@@ -510,6 +530,7 @@ class DecodeEngine:
         self.sin = torch.as_tensor(sin).to(dev)
         nl, nh, hd = cfg.num_hidden_layers, cfg.num_attention_heads, cfg.head_dim
         self.heads_split = self.split is not None and self.split.heads
+        self.peer_allreduce = False  # the head split's all-reduces through peer memory
         self.nh_local = self.split.h_local if self.heads_split else nh  # heads in this rank's cache
         # with the column split one extra slot takes the padding rows of a prefill whose
         # token count is below another rank's (their K/V land there and are never read)
@@ -539,6 +560,11 @@ class DecodeEngine:
             # ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
             if self.heads_split and os.environ.get("ORCHARD_PEER_ALLREDUCE", "1") != "0":
                 peer = _PeerAllReduce(group, self.split.world, self.split.rank, min(max_batch, 8) * H, dev)
+                if not peer.ok:
+                    import warnings
+                    warnings.warn("peer-memory all-reduce failed its self-test; the head split uses NCCL")
+                    peer = None
+            self.peer_allreduce = peer is not None
             self._comm = _NcclComm(group, self.split.world, self.split.rank, peer)
         self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         torch.cuda.synchronize(dev)

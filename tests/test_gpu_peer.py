@@ -2,24 +2,23 @@
 
 Its job is to sum a buffer over the GPUs of a box, but its arithmetic and its waits can be
 checked with one process: two regions on this GPU stand for rank 0's and rank 1's, rank 1's
-slot and flags are written from the host (as rank 1's kernel would write them over NVLink),
-and one launch as rank 0 must return x0 + x1 bit for bit, on both banks of slots, and write
-its own chunk and flags into both regions. A third call whose rank-1 flags nobody sets must
-give up after its bounded wait and report device check bit 512, with the context still
-usable. The layout constants follow orchard_b200/csrc/peer_allreduce.cu (header 256 bytes,
-flags [8][64] u32, slots from byte 4096: [bank][rank][cap] fp32). The two-GPU form runs in
-tests/test_gpu_split.py.
+slot is written from the host (as rank 1's kernel would write it over NVLink: each 64-bit
+word the call number over the fp32 bits), and one launch as rank 0 must return x0 + x1 bit
+for bit, on both banks of slots, and write its own words into both regions. A third call
+whose rank-1 words nobody writes must give up after its bounded wait and report device
+check bit 512, with the context still usable. The layout follows
+orchard_b200/csrc/peer_allreduce.cu (header 4096 bytes, then [bank][rank][cap] 64-bit
+words). The two-GPU form runs in tests/test_gpu_split.py.
 """
 
 import ctypes as C
 
-import numpy as np
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
-FLAGS, SLOTS, MAXB = 256, 4096, 64
+SLOTS = 4096
 
 
 @pytest.fixture(scope="module")
@@ -32,17 +31,19 @@ def lib():
 
 def _region(lib, world, cap):
     n = lib.lib().orch_peer_region_bytes(world, cap)
-    t = torch.zeros(n // 4 + 64, dtype=torch.int32, device="cuda")  # 256-byte aligned by torch
+    assert n == SLOTS + 2 * world * cap * 8
+    t = torch.zeros(n // 8, dtype=torch.int64, device="cuda")  # 256-byte aligned by torch
     assert t.data_ptr() % 256 == 0
     return t
 
 
-def _seed(region, bank, q, world, cap, data, flag_value, nblocks):
-    f = region.view(torch.float32)
-    off = (SLOTS + ((bank * world + q) * cap) * 4) // 4
-    f[off:off + data.numel()] = data.reshape(-1)
-    for b in range(nblocks):
-        region[FLAGS // 4 + q * MAXB + b] = flag_value
+def _words(x, call_no):
+    return (x.reshape(-1).view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (call_no << 32)
+
+
+def _slot(region, bank, q, world, cap, n):
+    off = (SLOTS + (bank * world + q) * cap * 8) // 8
+    return region[off:off + n]
 
 
 def test_peer_allreduce_sums_seeded_peer_bit_exact(lib):
@@ -52,33 +53,29 @@ def test_peer_allreduce_sums_seeded_peer_bit_exact(lib):
     bases = (C.c_void_p * 2)(A.data_ptr(), B.data_ptr())
     s = torch.cuda.current_stream().cuda_stream
     g = torch.Generator(device="cuda").manual_seed(7)
-    rows = 3
-    n = rows * H
-    nblocks = -(-(n // 4) // 1024)
-    for call_no in (1, 2):  # bank 1, then bank 0
+    for call_no, rows in ((1, 3), (2, 8), (3, 1)):  # banks 1, 0, 1; 1..64 blocks
+        n = rows * H
         x0 = torch.randn((rows_max, H), generator=g, device="cuda")
         x1 = torch.randn((rows, H), generator=g, device="cuda")
         tail = x0[rows:].clone()
-        _seed(A, call_no & 1, 1, world, cap, x1, call_no, nblocks)
+        _slot(A, call_no & 1, 1, world, cap, n).copy_(_words(x1, call_no))
         want = x0[:rows] + x1
         sent = x0[:rows].clone()
         lib.call("orch_peer_allreduce", C.addressof(bases), 0, world, cap, x0, n, s)
         torch.cuda.synchronize()
         assert torch.equal(x0[:rows], want)
-        assert torch.equal(x0[rows:], tail)  # rows past n untouched
-        assert int(A[0].item()) == call_no  # rank 0's call counter advanced once
-        # rank 0's chunk and flags landed in "rank 1's" region too
-        fb = B.view(torch.float32)
-        off = (SLOTS + ((call_no & 1) * world * cap) * 4) // 4
-        assert torch.equal(fb[off:off + n], sent.reshape(-1))
-        assert all(int(B[FLAGS // 4 + b].item()) == call_no for b in range(nblocks))
+        assert torch.equal(x0[rows:], tail)  # values past n untouched
+        assert int(A[0].item()) & 0xFFFFFFFF == call_no  # rank 0's call counter advanced once
+        # rank 0's words landed in "rank 1's" region as well as in its own
+        assert torch.equal(_slot(B, call_no & 1, 0, world, cap, n), _words(sent, call_no))
+        assert torch.equal(_slot(A, call_no & 1, 0, world, cap, n), _words(sent, call_no))
     flags = C.c_uint32(0)
     lib.call("orch_device_check", C.byref(flags), s)
     assert flags.value == 0
 
 
 def test_peer_allreduce_bounded_wait_reports_bit_512(lib):
-    """Rank 1's flags stay behind: the call gives up after its bounded wait (~5 s), flags bit
+    """Rank 1's words never arrive: the call gives up after its bounded wait (~5 s), flags bit
     512 and returns; the GPU keeps working."""
     world, cap = 2, 4096
     A, B = _region(lib, world, cap), _region(lib, world, cap)
