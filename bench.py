@@ -475,6 +475,62 @@ def time_head_split(cfg, dev, batches, steps, warmup, world, check_steps=8):
     return out
 
 
+def time_allreduce(dev, world, rows_list=(1, 8, 64), calls=32):
+    """The head split's all-reduce of fp32 residual rows [rows, 4096] alone: NCCL against the
+    peer-memory kernel (orch_peer_allreduce), `calls` dependent calls captured in one CUDA
+    graph, us per call (max over ranks), and the bytes each rank sends over NVLink per call
+    (NCCL ring: 2 (world - 1) / world of the buffer; the peer kernel: a 64-bit word per value
+    to each other rank)."""
+    import torch
+    import torch.distributed as dist
+
+    from orchard_b200.model import _PeerAllReduce
+    H = CFG7B["hidden_size"]
+    peer = _PeerAllReduce(dist.group.WORLD, world, dist.get_rank(), max(rows_list) * H, dev)
+    out = {"calls_per_graph": calls, "peer_self_test": peer.ok}
+    x = torch.randn((max(rows_list), H), device=dev) * 1e-3
+    for rows in rows_list:
+        n = rows * H
+        res = {}
+        for kind in ("nccl", "peer"):
+            if kind == "peer" and not peer.ok:
+                continue
+
+            def one():
+                if kind == "nccl":
+                    dist.all_reduce(x[:rows], op=dist.ReduceOp.SUM)
+                else:
+                    peer(x, n)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    one()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(calls):
+                    one()
+            g.replay()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize(dev)
+            t = torch.tensor([a.elapsed_time(b) / calls * 1000.0], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sent = 8 * n * (world - 1) if kind == "peer" else 4 * n * 2 * (world - 1) / world
+            res[kind] = {"us": round(float(t.item()), 2), "sent_bytes": int(sent),
+                         "GBps_out": round(sent / (float(t.item()) * 1e-6) / 1e9, 1)}
+            del g
+        out[str(rows)] = res
+    torch.cuda.synchronize(dev)
+    return out
+
+
 class OracleStepSample:
     """The oracle's decode step (the reference's arithmetic restated in NumPy) on the host
     cores, measured in bounded samples: one sample is one of the 32 layers of a batch-B step
@@ -672,6 +728,10 @@ def run_ours(args):
             hs = {"error": repr(e)[:300]}
             torch.cuda.empty_cache()
         line["head_split"] = hs
+        try:
+            line["allreduce_fp32_rows"] = time_allreduce(dev, world)
+        except Exception as e:
+            line["allreduce_fp32_rows"] = {"error": repr(e)[:300]}
         llm = build_model(cfg, dev, max_b, seed=1234 + rank)
         eng = llm.engine
         llm.prefill(prompts)
