@@ -749,6 +749,8 @@ class DecodeEngine:
         small = M <= _lib.lib().orch_gemv_max_rows()  # the GEMV normalises its own rows
         if self.heads_split:  # norm (above 8 rows) + qkv, attention, o, norm + gate/up, down
             per_layer = 5 + (0 if small else 2)
+            if self.peer_allreduce and M * self.cfg.hidden_size <= self._comm.peer.max_floats:
+                per_layer += 2  # the two all-reduces are this library's kernel
             if _lib.lib().orch_attention_workspace_bytes(M, self.nh_local, self.cfg.head_dim, self.max_seq) > 0:
                 per_layer += 1
             return 1 + per_layer * len(self.layers) + (4 if logits else 0)
