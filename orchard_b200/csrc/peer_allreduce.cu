@@ -29,7 +29,7 @@
 namespace orch {
 
 constexpr int kArMaxRanks = 8;
-constexpr int kArMaxBlocks = 64;
+constexpr int kArMaxBlocks = 296;  // two blocks per SM: always co-resident (62 registers x 256 threads)
 constexpr int kArThreads = 256;
 constexpr size_t kArSlotsOff = 4096;  // after the header: call counter, block counter
 
@@ -176,7 +176,7 @@ extern "C" int orch_peer_allreduce(void* const* bases, uint32_t rank, uint32_t w
   a.world = (int)world;
   a.npairs = (int)(n / 2);
   a.cap2 = max_floats / 2;
-  // a thread per pair of values, at most 64 blocks (larger buffers loop)
+  // a thread per pair of values, at most two blocks per SM (larger buffers loop)
   const int nb = std::min(kArMaxBlocks, std::max(1, (a.npairs + kArThreads - 1) / kArThreads));
   ORCH_CUDA(launch_k(peer_allreduce_kernel, dim3(nb), dim3(kArThreads), 0, as_stream(stream), dim3(0, 0, 0), a));
   return check_launch("peer_allreduce");

@@ -555,11 +555,11 @@ class DecodeEngine:
         if self.split is not None:
             self._split_ops = _CudaSplitOps(self)
             peer = None
-            # the head split's all-reduces through peer memory for up to 8 rows (at 64 rows
-            # NCCL measured faster on two GPUs: 4.76 against 5.16 ms per step);
-            # ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
+            # the head split's all-reduces of decode rows through peer memory (on two GPUs
+            # 4.8 / 5.2 / 9.5 us per call at 1 / 8 / 64 rows against NCCL's 15.2 / 16.8 / 19.9);
+            # prefill chunks take NCCL. ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
             if self.heads_split and os.environ.get("ORCHARD_PEER_ALLREDUCE", "1") != "0":
-                peer = _PeerAllReduce(group, self.split.world, self.split.rank, min(max_batch, 8) * H, dev)
+                peer = _PeerAllReduce(group, self.split.world, self.split.rank, max_batch * H, dev)
                 if not peer.ok:
                     import warnings
                     warnings.warn("peer-memory all-reduce failed its self-test; the head split uses NCCL")

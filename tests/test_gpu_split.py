@@ -125,10 +125,10 @@ def _ar_rank(rank, world, port, q):
         from orchard_b200._lib import call
         from orchard_b200.model import _PeerAllReduce
         call("orch_init", rank, None)
-        H, rows_max = 4096, 8
+        H, rows_max = 4096, 64
         ar = _PeerAllReduce(dist.group.WORLD, world, rank, rows_max * H, dev)
-        ok = []
-        for it, rows in enumerate([1, 8, 3, 8, 1, 2, 5]):  # block counts 1..8, both banks
+        ok = [ar.ok]
+        for it, rows in enumerate([1, 64, 3, 8, 64, 2, 37]):  # 8..296 blocks, both banks
             g = torch.Generator(device=dev).manual_seed(1000 * it + rank)
             x = torch.randn((rows_max, H), generator=g, device=dev)
             parts = [torch.empty((rows, H), device=dev) for _ in range(world)]
@@ -153,7 +153,7 @@ def _ar_rank(rank, world, port, q):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_peer_allreduce_two_gpus_bit_exact():
     """orch_peer_allreduce over two GPUs equals the rank-ordered fp32 sum of the gathered
-    inputs, bit for bit, on every rank, over calls of 1..8 rows (both banks of slots)."""
+    inputs, bit for bit, on every rank, over calls of 1..64 rows (both banks of slots)."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
