@@ -433,8 +433,8 @@ def time_head_split(cfg, dev, batches, steps, warmup, world, check_steps=8):
     llm.prefill(prompts)
     sp = eng.split
     out = {"heads_per_rank": sp.h_local, "by_global_batch": {},
-           "allreduce": ("peer-memory kernel (orch_peer_allreduce) for decode steps, NCCL for prefill chunks"
-                         if eng.peer_allreduce else "NCCL")}
+           "allreduce": (f"peer-memory kernel (orch_peer_allreduce) up to {eng._comm.peer.max_floats // cfg['hidden_size']}"
+                         " rows, NCCL above" if eng.peer_allreduce else "NCCL")}
     check = None
     if check_steps:
         last = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)

@@ -556,10 +556,15 @@ class DecodeEngine:
             self._split_ops = _CudaSplitOps(self)
             peer = None
             # the head split's all-reduces of decode rows through peer memory (on two GPUs
-            # 4.8 / 5.2 / 9.5 us per call at 1 / 8 / 64 rows against NCCL's 15.2 / 16.8 / 19.9);
-            # prefill chunks take NCCL. ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
+            # 4.8 / 5.2 / 9.5 us per call at 1 / 8 / 64 rows against NCCL's 15.2 / 16.8 / 19.9).
+            # The kernel sends every value to every other rank as a 64-bit word, 8 n (world - 1)
+            # bytes per call: it takes the row counts that keep that within 2.5 MiB (64 rows on
+            # two GPUs, 26 on four, 11 on eight); larger ones and prefill chunks take NCCL.
+            # ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
             if self.heads_split and os.environ.get("ORCHARD_PEER_ALLREDUCE", "1") != "0":
-                peer = _PeerAllReduce(group, self.split.world, self.split.rank, max_batch * H, dev)
+                W = self.split.world
+                rows = min(max_batch, max(1, (5 << 19) // (8 * H * (W - 1))))
+                peer = _PeerAllReduce(group, W, self.split.rank, rows * H, dev)
                 if not peer.ok:
                     import warnings
                     warnings.warn("peer-memory all-reduce failed its self-test; the head split uses NCCL")
