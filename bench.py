@@ -477,10 +477,11 @@ def time_head_split(cfg, dev, batches, steps, warmup, world, check_steps=8):
 
 def time_allreduce(dev, world, rows_list=(1, 8, 64), calls=32):
     """The head split's all-reduce of fp32 residual rows [rows, 4096] alone: NCCL against the
-    peer-memory kernel (orch_peer_allreduce), `calls` dependent calls captured in one CUDA
-    graph, us per call (max over ranks), and the bytes each rank sends over NVLink per call
-    (NCCL ring: 2 (world - 1) / world of the buffer; the peer kernel: a 64-bit word per value
-    to each other rank)."""
+    peer-memory kernel (orch_peer_allreduce; its automatic choice, and its two-shot form
+    forced), `calls` dependent calls captured in one CUDA graph, us per call (max over
+    ranks), and the bytes each rank sends over NVLink per call (NCCL ring: 2 (world - 1) /
+    world of the buffer; the peer kernel a 64-bit word per value: one shot to each other
+    rank, two shots 2 (world - 1) / world of the buffer)."""
     import torch
     import torch.distributed as dist
 
@@ -492,15 +493,15 @@ def time_allreduce(dev, world, rows_list=(1, 8, 64), calls=32):
     for rows in rows_list:
         n = rows * H
         res = {}
-        for kind in ("nccl", "peer"):
-            if kind == "peer" and not peer.ok:
+        for kind in ("nccl", "peer", "peer_two_shot"):
+            if kind != "nccl" and not peer.ok:
                 continue
 
             def one():
                 if kind == "nccl":
                     dist.all_reduce(x[:rows], op=dist.ReduceOp.SUM)
                 else:
-                    peer(x, n)
+                    peer(x, n, algo=2 if kind == "peer_two_shot" else 0)
             side = torch.cuda.Stream(dev)
             side.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(side):
@@ -522,7 +523,8 @@ def time_allreduce(dev, world, rows_list=(1, 8, 64), calls=32):
             torch.cuda.synchronize(dev)
             t = torch.tensor([a.elapsed_time(b) / calls * 1000.0], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            sent = 8 * n * (world - 1) if kind == "peer" else 4 * n * 2 * (world - 1) / world
+            one_shot = kind == "peer" and (world <= 2 or 8 * n * (world - 1) <= (1 << 20))
+            sent = 8 * n * (world - 1) if one_shot else (16 if kind != "nccl" else 8) * n * (world - 1) / world
             res[kind] = {"us": round(float(t.item()), 2), "sent_bytes": int(sent),
                          "GBps_out": round(sent / (float(t.item()) * 1e-6) / 1e9, 1)}
             del g

@@ -303,14 +303,17 @@ int orch_embed_rows(const int32_t* ids, const void* table, int table_dt, float* 
  * x[0..n) over the ranks in place: bases[q] is rank q's region as mapped here (own included),
  * the same world and max_floats the regions were sized with; n <= max_floats, both multiples
  * of 4; every rank makes the same calls in the same order. The result is the same bits on
- * every rank (slots added in rank order). A wait for a peer that runs out (~5 s) sets device
- * check bit 512. Regions and mappings live until orch_ipc_close / orch_free. */
+ * every rank (slots added in rank order). algo 1: one shot (every rank sends its whole buffer
+ * to every rank, 8 n (world - 1) bytes out); 2: two shots (reduce-scatter then all-gather,
+ * 16 n (world - 1) / world bytes out, one more NVLink crossing); 0: one shot on two ranks or
+ * while it sends at most 1 MiB, two shots otherwise. A wait for a peer that runs out (~5 s)
+ * sets device check bit 512. Regions and mappings live until orch_ipc_close / orch_free. */
 size_t orch_peer_region_bytes(uint32_t world, uint32_t max_floats);
 int orch_ipc_handle(void* base, void* handle_out);
 int orch_ipc_open(const void* handle, void** base_out);
 int orch_ipc_close(void* base);
 int orch_peer_allreduce(void* const* bases, uint32_t rank, uint32_t world, uint32_t max_floats,
-                        float* x, uint32_t n, void* stream);
+                        float* x, uint32_t n, int algo, void* stream);
 
 #ifdef __cplusplus
 }

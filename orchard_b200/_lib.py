@@ -103,7 +103,7 @@ _SIGS = {
     "orch_ipc_handle": (_i32, [_vp, _vp]),
     "orch_ipc_open": (_i32, [_vp, C.POINTER(_vp)]),
     "orch_ipc_close": (_i32, [_vp]),
-    "orch_peer_allreduce": (_i32, [_vp, _u32, _u32, _u32, _vp, _u32, _vp]),
+    "orch_peer_allreduce": (_i32, [_vp, _u32, _u32, _u32, _vp, _u32, _i32, _vp]),
 }
 
 _lock = threading.Lock()

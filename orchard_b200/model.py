@@ -427,22 +427,25 @@ class _PeerAllReduce:
         self.ok = bool(ok.item())
 
     def _self_test(self, device) -> bool:
+        """Known sums at the largest size and at one row, twice each (both banks of slots):
+        the algorithms the automatic choice takes at this world size."""
         import ctypes as C
-        n = self.max_floats - self.max_floats % 4
-        pattern = (1 + torch.arange(n, device=device) % 7).float()
-        want = pattern * (self.world * (self.world + 1) // 2)
         good = True
-        for _ in range(2):
-            x = pattern * (self.rank + 1)
-            self(x, n)
-            torch.cuda.synchronize(device)
-            good = good and bool(torch.equal(x, want))
+        for n in (self.max_floats - self.max_floats % 4, min(4096, self.max_floats) // 4 * 4):
+            pattern = (1 + torch.arange(n, device=device) % 7).float()
+            want = pattern * (self.world * (self.world + 1) // 2)
+            for _ in range(2):
+                x = pattern * (self.rank + 1)
+                self(x, n)
+                torch.cuda.synchronize(device)
+                good = good and bool(torch.equal(x, want))
         flags = C.c_uint32(0)
         call("orch_device_check", C.byref(flags), _stream())
         return good and (flags.value & 512) == 0
 
-    def __call__(self, x, n: int):
-        call("orch_peer_allreduce", self.bases_addr, self.rank, self.world, self.max_floats, ptr(x), n, _stream())
+    def __call__(self, x, n: int, algo: int = 0):
+        call("orch_peer_allreduce", self.bases_addr, self.rank, self.world, self.max_floats, ptr(x), n, algo,
+             _stream())
 
 
 class _NcclComm:
@@ -556,15 +559,11 @@ class DecodeEngine:
             self._split_ops = _CudaSplitOps(self)
             peer = None
             # the head split's all-reduces of decode rows through peer memory (on two GPUs
-            # 4.8 / 5.2 / 9.5 us per call at 1 / 8 / 64 rows against NCCL's 15.2 / 16.8 / 19.9).
-            # The kernel sends every value to every other rank as a 64-bit word, 8 n (world - 1)
-            # bytes per call: it takes the row counts that keep that within 2.5 MiB (64 rows on
-            # two GPUs, 26 on four, 11 on eight); larger ones and prefill chunks take NCCL.
-            # ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
+            # 4.8 / 5.2 / 9.5 us per call at 1 / 8 / 64 rows against NCCL's 15.2 / 16.8 / 19.9;
+            # on more GPUs the larger rows take the kernel's two-shot form); prefill chunks take
+            # NCCL. ORCHARD_PEER_ALLREDUCE=0: NCCL for every size
             if self.heads_split and os.environ.get("ORCHARD_PEER_ALLREDUCE", "1") != "0":
-                W = self.split.world
-                rows = min(max_batch, max(1, (5 << 19) // (8 * H * (W - 1))))
-                peer = _PeerAllReduce(group, W, self.split.rank, rows * H, dev)
+                peer = _PeerAllReduce(group, self.split.world, self.split.rank, max_batch * H, dev)
                 if not peer.ok:
                     import warnings
                     warnings.warn("peer-memory all-reduce failed its self-test; the head split uses NCCL")

@@ -137,7 +137,7 @@ def _ar_rank(rank, world, port, q):
             for p in parts[1:]:
                 want += p  # rank order, fp32: the kernel's order
             tail = x[rows:].clone()
-            ar(x, rows * H)
+            ar(x, rows * H, algo=1 + it % 2)  # one shot and two shots in turn
             torch.cuda.synchronize(dev)
             ok.append(bool(torch.equal(x[:rows], want)) and bool(torch.equal(x[rows:], tail)))
         import ctypes as C
@@ -153,7 +153,8 @@ def _ar_rank(rank, world, port, q):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_peer_allreduce_two_gpus_bit_exact():
     """orch_peer_allreduce over two GPUs equals the rank-ordered fp32 sum of the gathered
-    inputs, bit for bit, on every rank, over calls of 1..64 rows (both banks of slots)."""
+    inputs, bit for bit, on every rank, over calls of 1..64 rows (both banks of slots), with
+    the one-shot and the two-shot form in turn."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
