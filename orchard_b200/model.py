@@ -385,9 +385,10 @@ class _CudaSplitOps:
 class _PeerAllReduce:
     """The head split's all-reduce of fp32 rows through peer memory (orch_peer_allreduce):
     this rank's region (up to ``max_floats`` floats per rank and bank) allocated and zeroed
-    here, exported by CUDA IPC, every other rank's region opened; a barrier makes sure no
-    rank writes into a region before it is zeroed. The regions stay mapped for the life of
-    the process."""
+    here, exported by CUDA IPC, every other rank's region opened; a collective makes sure no
+    rank writes into a region before it is zeroed. ``ok`` is False on every rank when any
+    rank could not map a region or got a wrong known sum. The regions stay mapped for the
+    life of the process."""
 
     def __init__(self, group, world: int, rank: int, max_floats: int, device):
         import ctypes as C
@@ -408,21 +409,31 @@ class _PeerAllReduce:
         dist.all_gather_into_tensor(every, mine, group=group)
         every = every.cpu().numpy()
         bases = []
-        for q in range(world):
-            if q == rank:
-                bases.append(base.value)
-                continue
-            h = (C.c_uint8 * 64)(*every[q * 64:(q + 1) * 64].tolist())
-            peer = C.c_void_p()
-            call("orch_ipc_open", C.addressof(h), C.byref(peer))
-            bases.append(peer.value)
-        self._bases = (C.c_void_p * world)(*bases)
+        opened = True
+        try:
+            for q in range(world):
+                if q == rank:
+                    bases.append(base.value)
+                    continue
+                h = (C.c_uint8 * 64)(*every[q * 64:(q + 1) * 64].tolist())
+                peer = C.c_void_p()
+                call("orch_ipc_open", C.addressof(h), C.byref(peer))
+                bases.append(peer.value)
+        except _lib.OrchardError:
+            opened = False
+        self._bases = (C.c_void_p * world)(*(bases if opened else [None] * world))
         self.bases_addr = C.addressof(self._bases)
         torch.cuda.synchronize(device)
-        dist.barrier(group=group)
-        # a known sum over every rank, twice (both banks of slots); the ranks agree on the
-        # outcome, and on a failure they all keep the library collective
-        ok = torch.tensor([1 if self._self_test(device) else 0], dtype=torch.int32, device=device)
+        # every rank mapped every region (or all of them give up), and none writes into a
+        # region before it is zeroed
+        ok = torch.tensor([1 if opened else 0], dtype=torch.int32, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        self.ok = bool(ok.item())
+        if not self.ok:
+            return
+        # known sums over every rank; the ranks agree on the outcome, and on a failure they
+        # all keep the library collective
+        ok.fill_(1 if self._self_test(device) else 0)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
         self.ok = bool(ok.item())
 
