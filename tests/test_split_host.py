@@ -10,7 +10,9 @@ The head split (``attention_head_split`` / ``ffn_head_split`` / ``vocab_head_spl
 checked the same way against the oracle's own layer (``OracleModel.layer_forward``, which
 restates orchard/model.py:78-195): two ranks with half of the attention heads (their Q/K/V
 rows, O columns and KV cache) each, all rows on both ranks, bit-identical residuals after
-the all-reduces.
+the all-reduces. The set-up of its peer-memory all-reduce is checked against a fake
+library: a rank that cannot map a region, or gets a wrong known sum, makes every rank keep
+NCCL.
 """
 
 import os
@@ -381,3 +383,54 @@ def test_head_split_two_gloo_ranks_match_oracle_layer():
         assert np.array_equal(res[r][0], res[0][0])
         assert np.array_equal(res[r][1], tok_ref)
     assert np.abs(res[0][0] - x_ref).max() / np.abs(x_ref).max() <= 1e-5
+
+
+# ------------------------------------------------------------------------------------------
+# the head split's peer all-reduce set-up: every rank keeps NCCL when any rank fails
+# ------------------------------------------------------------------------------------------
+
+def _peer_setup_rank(rank, world, port, fail_rank, fail_test_rank, q):
+    """One gloo rank building _PeerAllReduce against a fake library: region size, IPC calls
+    and the self-test are stubbed; `fail_rank` fails to map a peer's region and
+    `fail_test_rank` gets a wrong known sum."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import orchard_b200.model as M
+        from orchard_b200 import _lib
+
+        class FakeLib:
+            def orch_peer_region_bytes(self, w, n):
+                return 4096 + 16 * w * n
+
+        def fake_call(name, *args):
+            if name == "orch_ipc_open" and rank == fail_rank:
+                raise _lib.OrchardError(name, 2, "mapping refused")
+            return 0
+
+        M._lib.lib = lambda: FakeLib()
+        M.call = fake_call
+        torch.cuda.synchronize = lambda *a, **k: None
+        M._PeerAllReduce._self_test = lambda self, dev: rank != fail_test_rank
+        p = M._PeerAllReduce(dist.group.WORLD, world, rank, 4096, "cpu")
+        q.put((rank, p.ok))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank,fail_test_rank,want", [(-1, -1, True), (1, -1, False), (-1, 0, False)])
+def test_peer_allreduce_setup_is_collective(fail_rank, fail_test_rank, want):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_setup_rank, args=(r, world, port, fail_rank, fail_test_rank, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got == {0: want, 1: want}
